@@ -1,0 +1,363 @@
+"""Benchmark: causal bf16 GQA attention forward+backward.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+A step is one forward (with saved log-sum-exp) plus one backward of
+``flash_attention`` on q [4, 32, 4096, 128], k/v [4, 8, 4096, 128], dO like q,
+bf16, causal -- the configuration BASELINE.json's headline metric is quoted on.
+Work per step uses the FlashAttention convention: forward 4*B*H*S^2*D / 2
+(causal half) = 5.50e11 FLOP, backward 2.5x forward; 1.924e12 FLOP per step.
+Inputs (320 MiB) exceed the 126 MB L2, so no flush is needed between steps.
+
+With N > 1 (torchrun, one process per GPU, NCCL) every rank runs the full
+config-2 workload on its own GPU (weak scaling over independent batch x kv-head
+units, no data-path collective); the time is the max over ranks and ``value``
+is the total FLOP of all ranks / that time.
+
+Also reported (rank 0, N = 1 only): the paged-decode HBM bandwidth on the
+config-4 workload (256 sequences, kv_len ~ U[512, 32768], page 16, H32/Hkv8,
+D128) and the CPU baseline -- the oracle's numpy restatement of the reference
+timed on one (batch, kv-head group) unit of config 2 and scaled by the unit count.
+``--impl reference`` times that CPU restatement alone (the reference is JAX on
+TPU; JAX is not installed, so its own CPU path cannot run here).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "tpu-native-pallas-flashattention_b200"))
+sys.path.insert(0, str(ROOT))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+B, H, HKV, S, D = 4, 32, 8, 4096, 128
+FWD_FLOP = 4.0 * B * H * S * S * D / 2
+BWD_FLOP = 2.5 * FWD_FLOP
+STEP_FLOP = FWD_FLOP + BWD_FLOP
+UNITS = B * HKV  # independent (batch, kv-head group) units of the step
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), float(d["bf16_tflops_sustained"]), "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+# --------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi sampling during the timed region (SM MHz and throttle reasons)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# --------------------------------------------------------------------------- CPU side
+def cpu_sample_step(q, k, v, do):
+    """One unit of config 2 through the oracle (naive fwd + closed-form VJP, fp32 numpy)."""
+    from oracle import attention_oracle as orc
+
+    out = orc.reference_attention(q, k, v, causal=True, dtype=np.float32)
+    orc.attention_vjp(q, k, v, do, causal=True, dtype=np.float32)
+    return out
+
+
+def cpu_baseline(steps: int = 1, warmup: int = 0):
+    rng = np.random.default_rng(0)
+    g = H // HKV
+    q = rng.standard_normal((1, g, S, D), dtype=np.float32)
+    k = rng.standard_normal((1, 1, S, D), dtype=np.float32)
+    v = rng.standard_normal((1, 1, S, D), dtype=np.float32)
+    do = rng.standard_normal((1, g, S, D), dtype=np.float32)
+    for _ in range(warmup):
+        cpu_sample_step(q, k, v, do)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        cpu_sample_step(q, k, v, do)
+    dt = (time.perf_counter() - t0) / steps
+    unit_flop = STEP_FLOP / UNITS
+    return {"value": unit_flop / dt / 1e12, "unit": "TFLOP/s", "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": f"1 of {UNITS} (batch, kv-head group) units of config 2 (4 q heads x 4096 x 128, causal), "
+                      f"numpy fp32 naive fwd + closed-form VJP, {dt:.2f} s/unit, scaled by unit FLOP"}
+
+
+# --------------------------------------------------------------------------- GPU side
+def make_inputs(dev, seed=0):
+    g = torch.Generator(device=dev).manual_seed(seed)
+    q = torch.randn((B, H, S, D), device=dev, generator=g).to(torch.bfloat16)
+    k = torch.randn((B, HKV, S, D), device=dev, generator=g).to(torch.bfloat16)
+    v = torch.randn((B, HKV, S, D), device=dev, generator=g).to(torch.bfloat16)
+    do = torch.randn((B, H, S, D), device=dev, generator=g).to(torch.bfloat16)
+    return q, k, v, do
+
+
+def step_device(pf, q, k, v, do):
+    qq, kk, vv = (t.detach().requires_grad_(True) for t in (q, k, v))
+    out = pf.flash_attention(qq, kk, vv, causal=True)
+    out.backward(do)
+    return qq.grad, kk.grad, vv.grad
+
+
+def time_kernels(pf, q, k, v, do, iters=5):
+    """Per-kernel-family device time (CUDA events on the launching stream)."""
+    from pallas_flash.flash_attention import _fwd, _bwd
+
+    scale = 1.0 / math.sqrt(D)
+    s = torch.cuda.current_stream()
+    out, lse = _fwd(q, k, v, True, scale, S, True)
+    _bwd(q, k, v, out, lse, do, True, scale, S)
+    torch.cuda.synchronize()
+    e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    fwd_ms = bwd_ms = 0.0
+    for _ in range(iters):
+        e[0].record(s)
+        out, lse = _fwd(q, k, v, True, scale, S, True)
+        e[1].record(s)
+        _bwd(q, k, v, out, lse, do, True, scale, S)
+        e[2].record(s)
+        torch.cuda.synchronize()
+        fwd_ms += e[0].elapsed_time(e[1])
+        bwd_ms += e[1].elapsed_time(e[2])
+    return fwd_ms / iters, bwd_ms / iters
+
+
+def paged_decode_bench(pf, dev, iters=10):
+    """Config 4: paged decode HBM GB/s (bytes = 4096 B per live token + q/out + table)."""
+    rng = np.random.default_rng(0)
+    nb, hq, hkv, ps, d = 256, 32, 8, 16, 128
+    lens = rng.integers(512, 32769, size=nb)
+    npages = [(int(x) + ps - 1) // ps for x in lens]
+    pool = int(math.ceil(1.1 * sum(npages)))
+    perm = rng.permutation(pool)
+    pps = max(npages)
+    table = np.zeros((nb, pps), np.int32)
+    off = 0
+    for b, n in enumerate(npages):
+        table[b, :n] = perm[off:off + n]
+        off += n
+    g = torch.Generator(device=dev).manual_seed(0)
+    kp = torch.empty((pool, hkv, ps, d), device=dev, dtype=torch.bfloat16).normal_(generator=g)
+    vp = torch.empty((pool, hkv, ps, d), device=dev, dtype=torch.bfloat16).normal_(generator=g)
+    q = torch.randn((nb, hq, 1, d), device=dev, generator=g).to(torch.bfloat16)
+    tt = torch.from_numpy(table).to(dev)
+    ll = torch.from_numpy(lens.astype(np.int32)).to(dev)
+    for _ in range(3):
+        pf.paged_flash_attention(q, kp, vp, tt, ll, max_context_len=32768)
+    torch.cuda.synchronize()
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(iters):
+        pf.paged_flash_attention(q, kp, vp, tt, ll, max_context_len=32768)
+    e1.record(s)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / iters
+    tokens = int(lens.sum())
+    nbytes = tokens * hkv * d * 2 * 2 + 2 * nb * hq * d * 2 + 4 * sum(npages)
+    del kp, vp
+    torch.cuda.empty_cache()
+    return {"workload": "config 4: 256 seqs, kv_len U[512,32768] (seed 0), page 16, H32/Hkv8/D128, bf16",
+            "tokens": tokens, "bytes": nbytes, "ms": ms, "GB/s": nbytes / ms / 1e6}
+
+
+def e2e_step(pf, host_in, host_out, dev):
+    """Public-API step from pinned host buffers: H2D inputs, fwd+bwd, D2H gradients."""
+    q, k, v, do = (h.to(dev, non_blocking=True) for h in host_in)
+    dq, dk, dv = step_device(pf, q, k, v, do)
+    for h, t in zip(host_out, (dq, dk, dv)):
+        h.copy_(t, non_blocking=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-extras", action="store_true", help="skip paged decode and CPU baseline")
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    config = {"workload": "config 2: causal GQA attention fwd+bwd", "batch": B, "heads": H, "kv_heads": HKV,
+              "seq_len": S, "head_dim": D, "causal": True, "l2": "inputs 320 MiB > L2, no flush",
+              "parallelism": f"replica x{args.gpus} (batch x kv-head units, no collective)"}
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        t0 = time.perf_counter()
+        cpu_baseline(steps=max(0, args.warmup))
+        cb = cpu_baseline(steps=args.steps)
+        print(json.dumps({
+            "impl": "reference", "metric": "fwd+bwd attention TFLOP/s", "value": cb["value"], "unit": "TFLOP/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": STEP_FLOP / (cb["value"] * 1e12) * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1))", "config": config,
+            "cpu_baseline": cb, "wall_s": time.perf_counter() - t0,
+            "e2e": {"value": cb["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "note": "oracle port (numpy fp32) of the reference's XLA-CPU path; JAX absent so the reference "
+                    "itself and its Pallas interpret mode cannot run"}))
+        return
+
+    import pallas_flash as pf
+    from pallas_flash import _lib
+
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
+    dev = torch.device("cuda", local_rank if world > 1 else 0)
+    torch.cuda.set_device(dev)
+    _lib.load_library()
+
+    q, k, v, do = make_inputs(dev, seed=rank)
+    for _ in range(max(3, args.warmup)):
+        step_device(pf, q, k, v, do)
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index) as clk:
+        barrier()
+        torch.cuda.synchronize()
+        e0.record(s)
+        for _ in range(args.steps):
+            step_device(pf, q, k, v, do)
+        e1.record(s)
+        torch.cuda.synchronize()
+        barrier()
+    ms = e0.elapsed_time(e1) / args.steps
+    ms_max = ms
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms_max = float(t.item())
+    value = STEP_FLOP * world / (ms_max * 1e-3) / 1e12
+
+    # end to end through the public API with pinned host buffers
+    host_in = [t.cpu().pin_memory() for t in (q, k, v, do)]
+    host_out = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in (q, k, v)]
+    for _ in range(2):
+        e2e_step(pf, host_in, host_out, dev)
+    torch.cuda.synchronize()
+    barrier()
+    e0.record(s)
+    e2e_steps = max(1, min(args.steps, 5))
+    for _ in range(e2e_steps):
+        e2e_step(pf, host_in, host_out, dev)
+    e1.record(s)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    h2d = sum(t.numel() * t.element_size() for t in host_in)
+    d2h = sum(t.numel() * t.element_size() for t in host_out)
+
+    fwd_ms, bwd_ms = time_kernels(pf, q, k, v, do)
+    hbm, tf_burst, tf_sust, src = peaks()
+    dom = ("backward (delta + dQ + dK/dV)", bwd_ms, BWD_FLOP) if bwd_ms >= fwd_ms else ("forward", fwd_ms, FWD_FLOP)
+    achieved = dom[2] / (dom[1] * 1e-3) / 1e12
+    traffic = None
+    tp = ROOT / "profiles" / "traffic.json"
+    if tp.exists():
+        traffic = json.loads(tp.read_text()).get("fwd_bwd_c2", {}).get("bwd" if dom[0].startswith("back") else "fwd")
+
+    line = {
+        "metric": "fwd+bwd attention TFLOP/s", "value": value, "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1))",
+        "config": config,
+        "roofline": {"bound": "tensor", "kernel": dom[0], "achieved": achieved, "peak": tf_burst,
+                     "unit": "TFLOP/s", "frac": achieved / tf_burst, "peak_source": f"{src} bf16 burst",
+                     "traffic": traffic, "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
+                     "fwd_tflops": FWD_FLOP / fwd_ms / 1e9, "bwd_tflops": BWD_FLOP / bwd_ms / 1e9,
+                     "fwd_frac": FWD_FLOP / fwd_ms / 1e9 / tf_burst},
+        "e2e": {"value": STEP_FLOP * world / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": 4 * args.steps,
+        "clocks": clk.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_extras:
+        pd = paged_decode_bench(pf, dev)
+        pd["frac_of_hbm"] = pd["GB/s"] / hbm
+        pd["hbm_peak_gbs"] = hbm
+        line["paged_decode"] = pd
+        line["cpu_baseline"] = cpu_baseline(steps=1)
+    if rank == 0:
+        print(json.dumps(line))
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

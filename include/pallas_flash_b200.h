@@ -1,0 +1,178 @@
+/*
+ * pallas_flash_b200.h -- C ABI of libpallas_flash_b200.so, the sm_100a (B200)
+ * attention kernels behind the pallas_flash Python API.
+ *
+ * Every entry point takes raw device pointers, plain integer shapes, scalars
+ * and the CUDA stream to launch on.  Nothing here allocates device memory:
+ * where a kernel needs scratch space (split-KV partials, the dQ accumulator)
+ * the caller passes a workspace and asks for its size first with the matching
+ * *_workspace_size function.  All tensors are dense row-major with the
+ * shapes stated below (the layouts of the reference's jax.Array operands).
+ *
+ * Return value: PF_OK (0) or one of the PF_ERR_* codes; pf_last_error()
+ * returns a static, human readable message for the most recent failure on
+ * the calling thread.
+ *
+ * Reference interfaces replaced (paths inside aabhimittal/TPU-Native-Pallas-
+ * FlashAttention):
+ *   pf_fwd              src/pallas_flash/flash_attention.py:162-227  (_flash_attention_call)
+ *   pf_bwd_preprocess   src/pallas_flash/flash_attention.py:363-365  (delta)
+ *   pf_bwd_dq           src/pallas_flash/flash_attention.py:276-311,379-398
+ *   pf_bwd_dkv          src/pallas_flash/flash_attention.py:314-351,403-436 (+ group_sum)
+ *   pf_bwd              src/pallas_flash/flash_attention.py:354-442  (_flash_attention_bwd_call)
+ *   pf_decode           src/pallas_flash/flash_attention.py:555-589  (flash_attention_decode)
+ *   pf_rope_fwd         src/pallas_flash/fused_rope.py:116-213       (flash_attention_rope)
+ *   pf_paged_decode     src/pallas_flash/paged.py:102-192            (paged_flash_attention)
+ *   pf_paged_write      src/pallas_flash/paged.py:205-223            (write_to_paged_cache)
+ *   pf_cache_write      src/pallas_flash/model.py:257-262,446-449    (_cache_write / ring slots)
+ *   pf_paged_gather     src/pallas_flash/paged.py:158-159            (the block-table index map)
+ */
+#ifndef PALLAS_FLASH_B200_H_
+#define PALLAS_FLASH_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Element types of q/k/v/o and of the cos/sin tables. */
+enum pf_dtype { PF_F32 = 0, PF_BF16 = 1, PF_F16 = 2 };
+
+/* Status codes. */
+enum pf_status {
+  PF_OK = 0,
+  PF_ERR_INVALID = 1,     /* bad shape / argument: the reference raises ValueError */
+  PF_ERR_UNSUPPORTED = 2, /* valid request this build has no kernel for           */
+  PF_ERR_CUDA = 3,        /* a CUDA runtime / driver call failed                   */
+  PF_ERR_DEVICE = 4,      /* a kernel recorded a device-side status (see below)    */
+  PF_ERR_WORKSPACE = 5    /* workspace pointer missing or too small                */
+};
+
+/* Device-side status bits, accumulated in a per-device word by the kernels
+ * instead of trapping; read (and optionally clear) with pf_device_status. */
+enum pf_device_bits {
+  PF_DEV_WAIT_TIMEOUT = 1, /* a bounded mbarrier wait gave up                     */
+  PF_DEV_BAD_PAGE = 2      /* a block-table entry was outside [0, num_pages)      */
+};
+
+const char* pf_last_error(void);
+/* Library version string, e.g. "0.1.0+sm100a". */
+const char* pf_version(void);
+/* Reads the device status word of the current device (synchronises the
+ * device); clears it when reset != 0. */
+int pf_device_status(int* bits_out, int reset);
+/* Which forward kernel family pf_fwd would use for these arguments:
+ * 1 = tcgen05/TMEM tensor-core kernel, 0 = fp32 SIMT kernel. */
+int pf_fwd_kernel_kind(int dtype, int head_dim);
+
+/* ---------------------------------------------------------------------------
+ * Prefill forward with saved log-sum-exp.
+ *   q   [B, H,   Sq, D]   k, v [B, Hkv, Sk, D]   o [B, H, Sq, D] (dtype of q)
+ *   lse [B, H, Sq] float32 (the reference's [B,H,Sq,1]); may be NULL.
+ * H % Hkv == 0 (query head h reads kv head h / (H/Hkv)).  Keys at positions
+ * >= kv_len (1 <= kv_len <= Sk) are masked and never read; causal applies
+ * q_pos >= k_pos with both sequences aligned at position 0.  Rows with no
+ * visible key give o = 0 and lse = 0.
+ * ------------------------------------------------------------------------- */
+int pf_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
+           int dtype, int B, int H, int Hkv, int Sq, int Sk, int D,
+           int causal, float sm_scale, int kv_len, void* stream);
+
+/* Forward with RoPE fused in: q and k are rotated inside the kernel with
+ * x*cos + rotate_half(x)*sin, q by rows of (q_cos, q_sin) [Sq, D] and k by
+ * rows of (k_cos, k_sin) [Sk, D] (table dtype tbl_dtype).  No lse output. */
+int pf_rope_fwd(const void* q, const void* k, const void* v,
+                const void* q_cos, const void* q_sin,
+                const void* k_cos, const void* k_sin, int tbl_dtype,
+                void* o, int dtype, int B, int H, int Hkv, int Sq, int Sk,
+                int D, int causal, float sm_scale, int kv_len, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Backward.  delta [B,H,Sq] f32 = sum_d o*do.
+ * dq like q, dk/dv like k/v (already summed over each GQA group).
+ * ------------------------------------------------------------------------- */
+int pf_bwd_preprocess(const void* o, const void* dout, float* delta,
+                      int dtype, int B, int H, int Sq, int D, void* stream);
+
+int pf_bwd_dq(const void* q, const void* k, const void* v, const void* dout,
+              const float* lse, const float* delta, void* dq,
+              int dtype, int B, int H, int Hkv, int Sq, int Sk, int D,
+              int causal, float sm_scale, int kv_len, void* stream);
+
+int pf_bwd_dkv(const void* q, const void* k, const void* v, const void* dout,
+               const float* lse, const float* delta, void* dk, void* dv,
+               int dtype, int B, int H, int Hkv, int Sq, int Sk, int D,
+               int causal, float sm_scale, int kv_len, void* stream);
+
+/* Whole backward (preprocess + dQ + dK/dV) in one call.  The workspace holds
+ * delta and, for the tensor-core path, an f32 dQ accumulator. */
+size_t pf_bwd_workspace_size(int dtype, int B, int H, int Hkv, int Sq, int Sk,
+                             int D);
+int pf_bwd(const void* q, const void* k, const void* v, const void* o,
+           const void* dout, const float* lse, void* dq, void* dk, void* dv,
+           int dtype, int B, int H, int Hkv, int Sq, int Sk, int D,
+           int causal, float sm_scale, int kv_len,
+           void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Single-query decode over a fixed-capacity cache.
+ *   q [B, H, 1, D]   k_cache, v_cache [B, Hkv, C, D]   o [B, H, 1, D]
+ * Attends cache positions [0, cache_len) (1 <= cache_len <= C); cache_len is
+ * a runtime scalar.  Split-KV: partial results go to the workspace.
+ * ------------------------------------------------------------------------- */
+size_t pf_decode_workspace_size(int B, int H, int Hkv, int C, int D);
+int pf_decode(const void* q, const void* k_cache, const void* v_cache, void* o,
+              int dtype, int B, int H, int Hkv, int C, int D, int cache_len,
+              float sm_scale, void* workspace, size_t workspace_bytes,
+              void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Paged decode.
+ *   q [B, H, 1, D]   k_pages, v_pages [num_pages, Hkv, page_size, D]
+ *   block_tables [B, pages_per_seq] int32   context_lens [B] int32 (device)
+ * Logical page p of sequence b lives in physical page block_tables[b, p];
+ * positions >= context_lens[b] are masked and their pages never read.
+ * max_context_len bounds context_lens (it sizes the split grid); pass
+ * pages_per_seq * page_size when unknown.
+ * ------------------------------------------------------------------------- */
+size_t pf_paged_decode_workspace_size(int B, int H, int Hkv, int page_size,
+                                      int max_context_len, int D);
+int pf_paged_decode(const void* q, const void* k_pages, const void* v_pages,
+                    const int32_t* block_tables, const int32_t* context_lens,
+                    void* o, int dtype, int B, int H, int Hkv, int num_pages,
+                    int page_size, int pages_per_seq, int D,
+                    int max_context_len, float sm_scale, void* workspace,
+                    size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Cache bookkeeping.
+ * pf_paged_write: for each sequence b of the batch, write one token's k/v
+ *   ([B, Hkv, 1, D] each) into page block_tables[b, positions[b] / page_size]
+ *   at offset positions[b] % page_size.  A physical page index outside
+ *   [0, num_pages) is clamped, as jax.lax.dynamic_update_slice clamps.
+ * pf_cache_write: write L tokens k/v [B, Hkv, L, D] into cache slots
+ *   (start + i) % C of k_cache/v_cache [B, Hkv, C, D] (a fixed cache when
+ *   start + L <= C, a ring buffer otherwise).
+ * pf_paged_gather: out[b, h, t, :] = pages[block_tables[b, t / ps], h,
+ *   t % ps, :] for t < pages_per_seq * ps (byte-exact copy; debug/oracle aid).
+ * ------------------------------------------------------------------------- */
+int pf_paged_write(void* k_pages, void* v_pages, const void* k, const void* v,
+                   const int32_t* block_tables, const int32_t* positions,
+                   int dtype, int B, int Hkv, int num_pages, int page_size,
+                   int pages_per_seq, int D, void* stream);
+
+int pf_cache_write(void* k_cache, void* v_cache, const void* k, const void* v,
+                   int dtype, int B, int Hkv, int C, int L, int D, int start,
+                   void* stream);
+
+int pf_paged_gather(const void* pages, const int32_t* block_tables, void* out,
+                    int dtype, int B, int Hkv, int num_pages, int page_size,
+                    int pages_per_seq, int D, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PALLAS_FLASH_B200_H_ */

@@ -1,0 +1,95 @@
+"""Backward parity on the GPU (port of the reference's tests/test_backward.py).
+
+Gradients of ``sum(flash_attention(q,k,v) * cot)`` through torch.autograd vs the
+oracle's closed-form VJP of the naive attention (what the reference compares
+with jax.grad).  fp32 bar: relative error < 1e-4 (tests/test_backward.py:65).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import pallas_flash as pf
+from oracle import attention_oracle as orc
+from conftest import randn, to_dev, to_np, widen, rel_err
+
+pytestmark = pytest.mark.gpu
+
+CASES = [(1, 2, 2, 128), (1, 2, 2, 256), (2, 4, 4, 256), (1, 4, 2, 256), (1, 4, 1, 256), (1, 2, 2, 200)]
+
+
+def inputs(B, H, Hkv, S, D, seed):
+    return (randn((B, H, S, D), seed), randn((B, Hkv, S, D), seed + 1),
+            randn((B, Hkv, S, D), seed + 2), randn((B, H, S, D), seed + 3))
+
+
+def grads(q, k, v, cot, causal, dtype=torch.float32, **kw):
+    tq, tk, tv = (to_dev(x, dtype).requires_grad_(True) for x in (q, k, v))
+    out = pf.flash_attention(tq, tk, tv, causal=causal, **kw)
+    (out.float() * to_dev(cot)).sum().backward()
+    return tq, tk, tv, out
+
+
+@pytest.mark.parametrize("case", CASES)
+@pytest.mark.parametrize("causal", [False, True])
+def test_grads_match_reference(case, causal):
+    B, H, Hkv, S = case
+    q, k, v, cot = inputs(B, H, Hkv, S, 128, 0)
+    tq, tk, tv, _ = grads(q, k, v, cot, causal)
+    want = orc.attention_vjp(q, k, v, cot, causal=causal)
+    for t, w in zip((tq, tk, tv), want):
+        assert t.grad.shape == t.shape and t.grad.dtype == torch.float32
+        g = to_np(t.grad)
+        assert np.all(np.isfinite(g))
+        assert rel_err(g, w) < 1e-4
+
+
+@pytest.mark.parametrize("block", [(64, 64), (128, 256), (256, 128)])
+def test_grads_block_sizes(block):
+    q, k, v, cot = inputs(1, 2, 2, 256, 128, 3)
+    tq, tk, tv, _ = grads(q, k, v, cot, True, block_q=block[0], block_k=block[1])
+    for t, w in zip((tq, tk, tv), orc.attention_vjp(q, k, v, cot, causal=True)):
+        assert rel_err(to_np(t.grad), w) < 1e-4
+
+
+def test_grads_bfloat16_finite_and_close():
+    q, k, v, cot = inputs(1, 4, 2, 384, 128, 4)
+    tq, tk, tv, _ = grads(q, k, v, cot, True, dtype=torch.bfloat16)
+    want = orc.attention_vjp(widen(tq), widen(tk), widen(tv), cot, causal=True)
+    for t, w in zip((tq, tk, tv), want):
+        assert t.grad.dtype == torch.bfloat16
+        g = to_np(t.grad)
+        assert np.all(np.isfinite(g))
+        assert rel_err(g, w) < 2e-2
+
+
+def test_kv_len_and_cross_lengths():
+    q, k, v = randn((1, 4, 90, 64), 5), randn((1, 2, 160, 64), 6), randn((1, 2, 160, 64), 7)
+    cot = randn((1, 4, 90, 64), 8)
+    tq, tk, tv = (to_dev(x).requires_grad_(True) for x in (q, k, v))
+    (pf.flash_attention(tq, tk, tv, causal=True, kv_len=100) * to_dev(cot)).sum().backward()
+    want = orc.attention_vjp(q, k, v, cot, causal=True, kv_len=100)
+    for t, w in zip((tq, tk, tv), want):
+        assert rel_err(to_np(t.grad), w) < 1e-4
+    assert float(tk.grad[:, :, 100:].abs().max()) == 0.0
+
+
+def test_value_and_grad_composes():
+    """tests/test_backward.py:94-105: loss value and finite grads."""
+    q, k, v, cot = inputs(1, 2, 2, 128, 128, 5)
+    tq, tk, tv, out = grads(q, k, v, cot, True)
+    value = float((out * to_dev(cot)).sum())
+    ref = float((orc.reference_attention(q, k, v, causal=True) * cot).sum())
+    assert abs(value - ref) <= 1e-4 + 1e-4 * abs(ref)
+    assert all(torch.isfinite(t.grad).all() for t in (tq, tk, tv))
+
+
+def test_golden_grads_on_gpu(golden):
+    for name, c in golden.items():
+        B, H, Hkv, Sq, Sk, D, causal, kv_len = (int(x) for x in c["meta"])
+        tq, tk, tv = (to_dev(c[n]).requires_grad_(True) for n in ("q", "k", "v"))
+        out = pf.flash_attention(tq, tk, tv, causal=bool(causal), sm_scale=float(c["scale"]),
+                                 kv_len=None if kv_len < 0 else kv_len)
+        (out * to_dev(c["do"])).sum().backward()
+        for t, n in ((tq, "dq"), (tk, "dk"), (tv, "dv")):
+            assert rel_err(to_np(t.grad), c[n]) < 1e-4, (name, n)

@@ -1,0 +1,166 @@
+"""Paged decode on the GPU (port of the reference's tests/test_paged.py) plus
+bit-exact block-table indexing checks."""
+
+import numpy as np
+import pytest
+import torch
+
+import pallas_flash as pf
+from pallas_flash import _lib
+from oracle import attention_oracle as orc
+from conftest import randn, to_dev, to_np, widen
+
+pytestmark = pytest.mark.gpu
+
+
+def scrambled_table(batch, pages_per_seq, num_pages, seed):
+    rng = np.random.default_rng(seed)
+    return np.stack([rng.choice(num_pages, size=pages_per_seq, replace=False) for _ in range(batch)]).astype(np.int32)
+
+
+@pytest.mark.parametrize("batch,n_heads,n_kv_heads,page_size,context_lens", [
+    (1, 2, 2, 64, [100]),
+    (3, 4, 2, 64, [10, 130, 200]),
+    (2, 4, 1, 128, [128, 5]),
+    (4, 2, 2, 32, [1, 33, 64, 90]),
+    (5, 8, 2, 16, [1, 16, 17, 300, 511]),
+])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_paged_matches_contiguous(batch, n_heads, n_kv_heads, page_size, context_lens, dtype):
+    dim = 128
+    pages_per_seq = max(context_lens) // page_size + 1
+    num_pages = max(32, batch * pages_per_seq)
+    q = randn((batch, n_heads, 1, dim), 0)
+    kp, vp = randn((num_pages, n_kv_heads, page_size, dim), 1), randn((num_pages, n_kv_heads, page_size, dim), 2)
+    table = scrambled_table(batch, pages_per_seq, num_pages, seed=batch)
+    tq, tkp, tvp = (to_dev(x, dtype) for x in (q, kp, vp))
+    out = pf.paged_flash_attention(tq, tkp, tvp, to_dev(table), torch.tensor(context_lens, dtype=torch.int32))
+    assert out.shape == q.shape
+    ref = orc.paged_attention(widen(tq), widen(tkp), widen(tvp), table, np.array(context_lens))
+    tol = 2e-3 if dtype == torch.float32 else 2e-2
+    assert np.max(np.abs(to_np(out) - ref)) < tol
+
+
+def test_pages_are_shareable():
+    dim, page_size, num_pages = 128, 64, 8
+    q1 = randn((1, 2, 1, dim), 7)
+    q = np.concatenate([q1, q1])
+    kp, vp = randn((num_pages, 2, page_size, dim), 8), randn((num_pages, 2, page_size, dim), 9)
+    out = pf.paged_flash_attention(to_dev(q), to_dev(kp), to_dev(vp),
+                                   torch.tensor([[3, 5], [3, 5]], dtype=torch.int32),
+                                   torch.tensor([100, 100], dtype=torch.int32))
+    assert torch.equal(out[0], out[1])
+
+
+def test_unwritten_pages_do_not_leak():
+    page_size, dim = 64, 128
+    kp = torch.cat([torch.ones((1, 2, page_size, dim)), torch.full((1, 2, page_size, dim), float("nan"))]).cuda()
+    q = torch.ones((1, 2, 1, dim), device="cuda")
+    out = pf.paged_flash_attention(q, kp, kp, torch.tensor([[0, 1]], dtype=torch.int32),
+                                   torch.tensor([page_size], dtype=torch.int32))
+    assert torch.isfinite(out).all()
+    assert torch.allclose(out, torch.ones_like(out), atol=1e-5)
+
+
+def test_trailing_table_entries_never_read():
+    """Entries past the context may be garbage (even out of range): never dereferenced."""
+    kp, vp = randn((4, 2, 16, 64), 1), randn((4, 2, 16, 64), 2)
+    q = randn((1, 4, 1, 64), 3)
+    table = np.array([[2, 0, 10**6, -5]], dtype=np.int32)
+    _lib.device_status(reset=True)
+    out = pf.paged_flash_attention(to_dev(q), to_dev(kp), to_dev(vp), to_dev(table),
+                                   torch.tensor([20], dtype=torch.int32))
+    kc = orc.gather_contiguous(kp, [2, 0], 2, 20)[None]
+    vc = orc.gather_contiguous(vp, [2, 0], 2, 20)[None]
+    ref = orc.reference_attention(q, kc, vc)
+    assert np.max(np.abs(to_np(out) - ref)) < 2e-3
+    assert _lib.device_status(reset=True) == 0
+
+
+def test_bad_page_id_is_flagged_not_faulted():
+    kp, vp = randn((4, 2, 16, 64), 1), randn((4, 2, 16, 64), 2)
+    q = randn((1, 4, 1, 64), 3)
+    _lib.device_status(reset=True)
+    pf.paged_flash_attention(to_dev(q), to_dev(kp), to_dev(vp), torch.tensor([[1, 99]], dtype=torch.int32),
+                             torch.tensor([20], dtype=torch.int32))
+    assert _lib.device_status(reset=True) & _lib.PF_DEV_BAD_PAGE
+
+
+def test_write_to_paged_cache_roundtrip():
+    page_size, dim, n_kv, num_pages, length = 32, 128, 2, 4, 70
+    k_pages, v_pages = pf.init_paged_cache(num_pages, n_kv, page_size, dim)
+    table = torch.tensor([0, 2, 1, 3], dtype=torch.int32)
+    ks, vs = randn((1, n_kv, length, dim), 11), randn((1, n_kv, length, dim), 12)
+    tks, tvs = to_dev(ks), to_dev(vs)
+    for pos in range(length):
+        k_pages, v_pages = pf.write_to_paged_cache(k_pages, v_pages, tks[:, :, pos:pos + 1],
+                                                   tvs[:, :, pos:pos + 1], table, pos)
+    q = randn((1, 2, 1, dim), 13)
+    out = pf.paged_flash_attention(to_dev(q), k_pages, v_pages, table[None], torch.tensor([length], dtype=torch.int32))
+    assert np.max(np.abs(to_np(out) - orc.reference_attention(q, ks, vs))) < 2e-3
+    # byte-exact placement against the oracle's writer
+    okp = np.zeros((num_pages, n_kv, page_size, dim), np.float32)
+    ovp = np.zeros_like(okp)
+    for pos in range(length):
+        orc.paged_write(okp, ovp, ks[:, :, pos:pos + 1], vs[:, :, pos:pos + 1], table.numpy(), pos)
+    assert np.array_equal(k_pages.cpu().numpy(), okp) and np.array_equal(v_pages.cpu().numpy(), ovp)
+
+
+def test_write_out_of_table_raises_index_error():
+    k_pages, v_pages = pf.init_paged_cache(4, 2, 32, 128)
+    x = torch.zeros((1, 2, 1, 128), device="cuda")
+    with pytest.raises(IndexError):
+        pf.write_to_paged_cache(k_pages, v_pages, x, x, torch.tensor([0, 1], dtype=torch.int32), 64)
+
+
+def test_gather_is_byte_exact():
+    pool = torch.randn((64, 4, 16, 128), device="cuda").to(torch.bfloat16)
+    table = scrambled_table(5, 12, 64, 3)
+    got = pf.gather_paged(pool, to_dev(table))
+    want = np.stack([orc.gather_contiguous(pool.view(torch.int16).cpu().numpy(), table[b], 12, 12 * 16)
+                     for b in range(5)])
+    assert np.array_equal(got.view(torch.int16).cpu().numpy(), want)
+
+
+def test_paged_equals_fixed_cache_bitwise():
+    """Same split schedule => paged decode over a scrambled pool == fixed-cache decode of the gather."""
+    B, H, Hkv, ps, D, pps = 4, 8, 2, 16, 128, 64
+    cap = ps * pps
+    num_pages = B * pps + 7
+    g = torch.Generator(device="cuda").manual_seed(5)
+    pool_k = torch.randn((num_pages, Hkv, ps, D), device="cuda", generator=g).to(torch.bfloat16)
+    pool_v = torch.randn((num_pages, Hkv, ps, D), device="cuda", generator=g).to(torch.bfloat16)
+    q = torch.randn((B, H, 1, D), device="cuda", generator=g).to(torch.bfloat16)
+    table = to_dev(scrambled_table(B, pps, num_pages, 9))
+    kc, vc = pf.gather_paged(pool_k, table), pf.gather_paged(pool_v, table)
+    for L in (cap, 700, 33):
+        paged = pf.paged_flash_attention(q, pool_k, pool_v, table, torch.full((B,), L, dtype=torch.int32),
+                                         max_context_len=cap)
+        fixed = pf.flash_attention_decode(q, kc, vc, L)
+        assert torch.equal(paged, fixed), L
+
+
+def test_c4_shape_sampled():
+    """BASELINE config 4 shape (page 16, H32/Hkv8/D128) on 16 sequences, ragged lengths."""
+    rng = np.random.default_rng(0)
+    B, H, Hkv, ps, D = 16, 32, 8, 16, 128
+    lens = rng.integers(512, 32769, size=B)
+    pages = [(int(L) + ps - 1) // ps for L in lens]
+    pool = int(np.ceil(1.1 * sum(pages)))
+    perm = rng.permutation(pool)
+    pps = max(pages)
+    table = np.zeros((B, pps), np.int32)
+    off = 0
+    for b, n in enumerate(pages):
+        table[b, :n] = perm[off:off + n]
+        off += n
+    g = torch.Generator(device="cuda").manual_seed(1)
+    kp = torch.randn((pool, Hkv, ps, D), device="cuda", generator=g).to(torch.bfloat16)
+    vp = torch.randn((pool, Hkv, ps, D), device="cuda", generator=g).to(torch.bfloat16)
+    q = torch.randn((B, H, 1, D), device="cuda", generator=g).to(torch.bfloat16)
+    out = pf.paged_flash_attention(q, kp, vp, to_dev(table), torch.tensor(lens, dtype=torch.int32))
+    for b in (0, 7, 15):
+        kc = pf.gather_paged(kp, to_dev(table[b:b + 1]))[:, :, :lens[b]]
+        vc = pf.gather_paged(vp, to_dev(table[b:b + 1]))[:, :, :lens[b]]
+        ref = orc.reference_attention(widen(q[b:b + 1]), widen(kc), widen(vc), dtype=np.float32)
+        assert np.max(np.abs(to_np(out[b:b + 1]) - ref)) < 2e-2

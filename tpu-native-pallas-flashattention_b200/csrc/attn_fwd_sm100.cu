@@ -1,0 +1,409 @@
+// attn_fwd_sm100.cu -- tensor-core (tcgen05 / TMEM / TMA) prefill forward for
+// bf16 and f16 inputs, head_dim 64 or 128, with the saved log-sum-exp.
+//
+// One CTA owns two 128-row query tiles of one (batch, head) and streams the
+// 128-key K/V tiles of the matching kv head (h / (H/Hkv), the GQA map of
+// flash_attention.py:187-190) through a TMA-fed shared-memory ring:
+//
+//   warp 0      TMA producer: Q0, Q1 once, then K_j / V_j per stage
+//   warp 1      MMA issuer (one elected thread) and TMEM owner:
+//                 S_w = Q_w K_j^T        (SS: both operands K-major in smem)
+//                 O_w += P_w V_j          (TS: P from TMEM, V MN-major in smem)
+//   warps 4-7   softmax for query tile 0 (TMEM lanes 0-127 = its rows)
+//   warps 8-11  softmax for query tile 1
+//
+// The two tiles ping-pong on the tensor core: while one warpgroup turns S
+// into P, the MMA warp runs the other tile's GEMMs.  S, O live in TMEM
+// (S0 | S1 | O0 | O1 = 512 columns at D = 128); P overwrites the first half of
+// its S buffer as packed 16-bit pairs and feeds the PV MMA straight from TMEM.
+// Softmax statistics are fp32 in the log2 domain; the running max used for
+// P is only raised when the row max grows by more than 2^8, so O in TMEM is
+// rescaled rarely (the final O / l is exact for any reference max).
+//
+// Masking follows the reference: keys >= kv_len are never loaded (the K/V
+// tensor maps end at kv_len, TMA zero-fills past it), causal masks
+// k_pos > q_pos with both sequences aligned at 0, kv blocks past kv_len or
+// the causal diagonal are skipped (flash_attention.py:136-147), rows with no
+// visible key write o = 0, lse = 0 (:150-159).
+#include <cuda.h>
+#include <type_traits>
+#include "common.cuh"
+#include "kernels.h"
+
+namespace pf {
+namespace {
+
+constexpr int kBM = 128;        // rows per query tile (= TMEM lanes)
+constexpr int kBN = 128;        // keys per kv tile
+constexpr int kThreads = 384;   // 12 warps
+constexpr float kRescaleThresh = 8.0f;  // log2 units
+
+template <int D>
+struct FwdCfg {
+  static constexpr int kBoxes = D / 64;                  // 64-column (128 B) TMA boxes
+  static constexpr int kTileBytes = kBM * D * 2;         // one 128 x D 16-bit tile
+  static constexpr int kStages = D == 128 ? 2 : 4;
+  static constexpr int kQOff = 0;                        // Q0, Q1
+  static constexpr int kKOff = 2 * kTileBytes;           // K stages
+  static constexpr int kVOff = kKOff + kStages * kTileBytes;
+  static constexpr int kBarOff = kVOff + kStages * kTileBytes;
+  static constexpr int kSmem = kBarOff + 256 + 1024;     // + barriers + alignment slack
+  // TMEM columns
+  static constexpr uint32_t kS0 = 0, kS1 = 128, kO0 = 256, kO1 = 256 + D;
+  static constexpr uint32_t kTmemCols = 512;
+};
+
+struct Bars {
+  uint64_t q;
+  uint64_t k_full[4], v_full[4], kv_empty[4];
+  uint64_t s_full[2], p_full[2], o_done[2];
+  uint32_t tmem_base;
+};
+
+// Descriptor for a K-major 128 x D tile stored as kBoxes swizzled boxes of
+// 128 rows x 128 B; k-step kk covers elements [16 kk, 16 kk + 16).
+template <int D>
+__device__ __forceinline__ uint64_t desc_kmajor(uint32_t tile_addr, int kk) {
+  const uint32_t addr = tile_addr + (kk >> 2) * (kBM * 128) + (kk & 3) * 32;
+  return smem_desc_sw128(addr, 16, 1024);
+}
+// Descriptor for V (B operand of P.V, MN-major): rows = keys, columns = d.
+// k-step kk covers keys [16 kk, 16 kk + 16) = 2 groups of 8 rows (SBO apart);
+// the next 64 columns live in the next box (LBO apart).
+template <int D>
+__device__ __forceinline__ uint64_t desc_v(uint32_t tile_addr, int kk) {
+  return smem_desc_sw128(tile_addr + kk * 16 * 128, kBN * 128, 1024);
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kThreads, 1)
+fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                 const __grid_constant__ CUtensorMap tm_v, T* __restrict__ out,
+                 float* __restrict__ lse, int B, int H, int Hkv, int Sq, int kv_len, int causal,
+                 float scale_log2, int n_qtiles) {
+  using Cfg = FwdCfg<D>;
+  constexpr int NS = Cfg::kStages;
+  constexpr int fmt = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
+  constexpr uint32_t idesc_qk = make_idesc_f16(fmt, kBM, kBN, 0, 0);
+  constexpr uint32_t idesc_pv = make_idesc_f16(fmt, kBM, D, 0, 1);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Bars* bars = reinterpret_cast<Bars*>(smem + Cfg::kBarOff);
+  const uint32_t sbase = smem_u32(smem);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+
+  // Heaviest (last, under causal) query tiles first; heads of one kv group
+  // adjacent so their shared K/V tiles meet in L2.
+  const int bh = blockIdx.x % (B * H);
+  const int qt = n_qtiles - 1 - blockIdx.x / (B * H);
+  const int b = bh / H, h = bh % H;
+  const int hk = h / (H / Hkv);
+  const int q_start = qt * 2 * kBM;
+  const int kvb = (kv_len + kBN - 1) / kBN;
+  int n_w[2];
+#pragma unroll
+  for (int w = 0; w < 2; ++w) {
+    const int t0 = q_start + w * kBM;
+    if (t0 >= Sq) {
+      n_w[w] = 0;
+    } else {
+      const int last = min(t0 + kBM - 1, Sq - 1);
+      n_w[w] = causal ? min(kvb, last / kBN + 1) : kvb;
+    }
+  }
+  const int n_max = max(n_w[0], n_w[1]);
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars->q, 1);
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&bars->k_full[s], 1);
+      mbar_init(&bars->v_full[s], 1);
+      mbar_init(&bars->kv_empty[s], 1);
+    }
+    for (int w = 0; w < 2; ++w) {
+      mbar_init(&bars->s_full[w], 1);
+      mbar_init(&bars->p_full[w], kBM);
+      mbar_init(&bars->o_done[w], 1);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&bars->tmem_base, Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------ producer ------------------------------
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+      const int active = (n_w[0] > 0) + (n_w[1] > 0);
+      mbar_expect_tx(&bars->q, active * Cfg::kTileBytes);
+      for (int w = 0; w < 2; ++w) {
+        if (n_w[w] == 0) continue;
+        for (int c = 0; c < Cfg::kBoxes; ++c)
+          tma_load_3d(smem + Cfg::kQOff + w * Cfg::kTileBytes + c * kBM * 128, &tm_q, &bars->q,
+                      c * 64, q_start + w * kBM, bh);
+      }
+      const int kv_plane = b * Hkv + hk;
+      for (int j = 0; j < n_max; ++j) {
+        const int s = j % NS;
+        if (j >= NS && !mbar_wait(&bars->kv_empty[s], ((j / NS) - 1) & 1)) break;
+        mbar_expect_tx(&bars->k_full[s], Cfg::kTileBytes);
+        for (int c = 0; c < Cfg::kBoxes; ++c)
+          tma_load_3d(smem + Cfg::kKOff + s * Cfg::kTileBytes + c * kBN * 128, &tm_k,
+                      &bars->k_full[s], c * 64, j * kBN, kv_plane);
+        mbar_expect_tx(&bars->v_full[s], Cfg::kTileBytes);
+        for (int c = 0; c < Cfg::kBoxes; ++c)
+          tma_load_3d(smem + Cfg::kVOff + s * Cfg::kTileBytes + c * kBN * 128, &tm_v,
+                      &bars->v_full[s], c * 64, j * kBN, kv_plane);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------ MMA issuer ----------------------------
+    if (lane == 0 && n_max > 0) {
+      bool ok = mbar_wait(&bars->q, 0);
+      tc_fence_after();
+      const uint32_t q_addr[2] = {sbase + Cfg::kQOff, sbase + Cfg::kQOff + Cfg::kTileBytes};
+      const uint32_t s_col[2] = {Cfg::kS0, Cfg::kS1};
+      const uint32_t o_col[2] = {Cfg::kO0, Cfg::kO1};
+      auto issue_s = [&](int w, int j) {
+        const uint32_t k_addr = sbase + Cfg::kKOff + (j % NS) * Cfg::kTileBytes;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)
+          umma_ss(tmem + s_col[w], desc_kmajor<D>(q_addr[w], kk), desc_kmajor<D>(k_addr, kk),
+                  idesc_qk, kk > 0 ? 1u : 0u);
+        umma_commit(&bars->s_full[w]);
+      };
+      auto issue_pv = [&](int w, int j) {
+        const uint32_t v_addr = sbase + Cfg::kVOff + (j % NS) * Cfg::kTileBytes;
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk)
+          umma_ts(tmem + o_col[w], tmem + s_col[w] + kk * 8, desc_v<D>(v_addr, kk), idesc_pv,
+                  (j > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&bars->o_done[w]);
+      };
+      for (int j = 0; ok && j <= n_max; ++j) {
+        const int s = j % NS;
+        const bool need_k = (j < n_w[0]) || (j < n_w[1]);
+        if (need_k) {
+          ok = mbar_wait(&bars->k_full[s], (j / NS) & 1);
+          if (!ok) break;
+          tc_fence_after();
+        }
+        if (j < n_w[0]) issue_s(0, j);
+        if (j >= 1 && j - 1 < n_w[1]) {
+          const int sp = (j - 1) % NS;
+          ok = mbar_wait(&bars->p_full[1], (j - 1) & 1) && mbar_wait(&bars->v_full[sp], ((j - 1) / NS) & 1);
+          if (!ok) break;
+          tc_fence_after();
+          issue_pv(1, j - 1);
+          umma_commit(&bars->kv_empty[sp]);  // last reader of stage j-1
+        }
+        if (j < n_w[1]) issue_s(1, j);
+        if (j < n_w[0]) {
+          ok = mbar_wait(&bars->p_full[0], j & 1) && mbar_wait(&bars->v_full[s], (j / NS) & 1);
+          if (!ok) break;
+          tc_fence_after();
+          issue_pv(0, j);
+          if (j >= n_w[1]) umma_commit(&bars->kv_empty[s]);
+        }
+      }
+    }
+  } else if (warp >= 4) {
+    // ------------------------------ softmax -------------------------------
+    const int w = (warp - 4) / 4;           // query tile of this warpgroup
+    const int quad = warp % 4;              // TMEM lane quadrant
+    const int row = quad * 32 + lane;       // row within the tile
+    const int qpos = q_start + w * kBM + row;
+    const int n = n_w[w];
+    const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
+    const uint32_t s_addr = lane_base + (w == 0 ? Cfg::kS0 : Cfg::kS1);
+    const uint32_t o_addr = lane_base + (w == 0 ? Cfg::kO0 : Cfg::kO1);
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n; ++j) {
+      if (!mbar_wait(&bars->s_full[w], j & 1)) { ok = false; break; }
+      tc_fence_after();
+      const int k0 = j * kBN;
+      const bool edge = (k0 + kBN > kv_len) || (causal && k0 + kBN - 1 > q_start + w * kBM);
+      // Visible-key count of this row in the tile: keys [k0, k0 + vis) survive
+      // both the kv_len and the causal mask.
+      int vis = kBN;
+      if (edge) {
+        vis = min(kBN, kv_len - k0);
+        if (causal) vis = min(vis, qpos - k0 + 1);
+        vis = max(vis, 0);
+      }
+      // Pass 1: row max over the visible scores.
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < kBN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(s_addr + c * 32, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (c * 32 + i < vis) mx = fmaxf(mx, __uint_as_float(r[i]));
+      }
+      mx *= scale_log2;
+      // Lazy rescale: raise the reference max only when it grew by > 2^8.
+      const bool upd = mx > m_run + kRescaleThresh;
+      const float alpha = upd ? fast_exp2(m_run - mx) : 1.f;  // 0 when m_run = -inf
+      if (upd) {
+        l_run *= alpha;
+        m_run = mx;
+      }
+      if (j > 0 && __any_sync(0xffffffffu, upd)) {
+        // PV of tile j-1 is complete: its commit preceded S_w(j)'s.
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(o_addr + c * 32, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+          tmem_st32(o_addr + c * 32, r);
+        }
+      }
+      // Pass 2: P = 2^(s*scale - m) packed to 16-bit pairs over the first half
+      // of the S columns (chunk c's source columns are consumed before any
+      // store reaches them).
+      const float msub = (m_run == -INFINITY) ? 0.f : m_run;
+      float rowsum = 0.f;
+#pragma unroll
+      for (int c = 0; c < kBN / 64; ++c) {
+        uint32_t ra[32], rb[32];
+        tmem_ld32(s_addr + c * 64, ra);
+        tmem_ld32(s_addr + c * 64 + 32, rb);
+        tmem_wait_ld();
+        uint32_t pk[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const uint32_t* src = i < 16 ? ra : rb;
+          const int ii = (i % 16) * 2;
+          const int col = c * 64 + 2 * i;
+          const float p0 = col < vis ? fast_exp2(fmaf(__uint_as_float(src[ii]), scale_log2, -msub)) : 0.f;
+          const float p1 = col + 1 < vis ? fast_exp2(fmaf(__uint_as_float(src[ii + 1]), scale_log2, -msub)) : 0.f;
+          rowsum += p0 + p1;
+          pk[i] = (fmt == 1) ? pack_bf16x2(p0, p1) : pack_f16x2(p0, p1);
+        }
+        tmem_st32(s_addr + c * 32, pk);
+      }
+      l_run += rowsum;
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&bars->p_full[w]);
+    }
+    // ------------------------------ epilogue ------------------------------
+    if (n > 0 && ok && mbar_wait(&bars->o_done[w], (n - 1) & 1)) {
+      tc_fence_after();
+      const bool empty = (l_run == 0.f);
+      const float inv = empty ? 0.f : 1.f / l_run;
+      T* orow = out + (((long)b * H + h) * Sq + qpos) * D;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(o_addr + c * 32, r);
+        tmem_wait_ld();
+        if (qpos < Sq) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float a0 = __uint_as_float(r[2 * i]) * inv, a1 = __uint_as_float(r[2 * i + 1]) * inv;
+            pk[i] = (fmt == 1) ? pack_bf16x2(a0, a1) : pack_f16x2(a0, a1);
+          }
+          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+        }
+      }
+      if (lse != nullptr && qpos < Sq)
+        lse[((long)b * H + h) * Sq + qpos] = empty ? 0.f : (m_run + log2f(l_run)) * kLn2;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, Cfg::kTmemCols);
+  }
+}
+
+// --------------------------------------------------------------------------
+// Host side: tensor maps through the driver entry point (no -lcuda needed).
+// --------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (fn == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// 3-D map over a [planes, rows_stride, D] tensor that exposes `rows` rows per
+// plane; box = 64 columns x 128 rows, 128-byte swizzle, zero fill past `rows`.
+bool make_map(CUtensorMap* m, const void* base, int dtype, int D, int rows, long row_stride_rows,
+              int planes) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (enc == nullptr) return false;
+  const CUtensorMapDataType dt =
+      dtype == PF_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)rows, (cuuint64_t)planes};
+  cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)row_stride_rows * D * 2};
+  cuuint32_t box[3] = {64, 128, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return enc(m, dt, 3, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <typename T, int D>
+cudaError_t launch_t(const FwdArgs& a) {
+  using Cfg = FwdCfg<D>;
+  CUtensorMap tq, tk, tv;
+  if (!make_map(&tq, a.q, a.dtype, D, a.Sq, a.Sq, a.B * a.H) ||
+      !make_map(&tk, a.k, a.dtype, D, a.kv_len, a.Sk, a.B * a.Hkv) ||
+      !make_map(&tv, a.v, a.dtype, D, a.kv_len, a.Sk, a.B * a.Hkv))
+    return cudaErrorInvalidValue;
+  auto kern = fwd_sm100_kernel<T, D>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
+  if (e != cudaSuccess) return e;
+  const int n_qtiles = (a.Sq + 2 * kBM - 1) / (2 * kBM);
+  dim3 grid((unsigned)(n_qtiles * a.B * a.H));
+  const float scale_log2 = a.sm_scale * kLog2e;
+  kern<<<grid, kThreads, Cfg::kSmem, a.stream>>>(tq, tk, tv, (T*)a.o, a.lse, a.B, a.H, a.Hkv, a.Sq,
+                                                 a.kv_len, a.causal, scale_log2, n_qtiles);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+bool fwd_sm100_supported(int dtype, int D) {
+  return (dtype == PF_BF16 || dtype == PF_F16) && (D == 64 || D == 128);
+}
+
+cudaError_t launch_fwd_sm100(const FwdArgs& a) {
+  if (a.dtype == PF_BF16) return a.D == 128 ? launch_t<__nv_bfloat16, 128>(a) : launch_t<__nv_bfloat16, 64>(a);
+  return a.D == 128 ? launch_t<__half, 128>(a) : launch_t<__half, 64>(a);
+}
+
+}  // namespace pf

@@ -1,0 +1,299 @@
+// capi.cu -- the extern "C" boundary of libpallas_flash_b200.so.
+//
+// Validates arguments with the reference's rules (the ValueError checks of
+// flash_attention.py:527-545, fused_rope.py:154-181, paged.py:129-149),
+// picks the kernel family and launches on the caller's stream.  Nothing here
+// allocates device memory; scratch comes from the caller's workspace.
+#include <cstdio>
+#include <cstring>
+#include <cstdarg>
+#include <type_traits>
+
+#include "common.cuh"
+#include "kernels.h"
+
+using namespace pf;
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int cuda_status(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return PF_OK;
+  return fail(PF_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+bool valid_dtype(int d) { return d == PF_F32 || d == PF_BF16 || d == PF_F16; }
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int check_attn_shapes(const char* fn, const void* q, const void* k, const void* v, int dtype,
+                      int B, int H, int Hkv, int Sq, int Sk, int D, int kv_len) {
+  if (!valid_dtype(dtype)) return fail(PF_ERR_INVALID, "%s: unknown dtype %d", fn, dtype);
+  if (q == nullptr || k == nullptr || v == nullptr) return fail(PF_ERR_INVALID, "%s: null input", fn);
+  if (B <= 0 || H <= 0 || Sq <= 0 || Sk <= 0 || D <= 0)
+    return fail(PF_ERR_INVALID, "%s: shapes must be positive (B=%d H=%d Sq=%d Sk=%d D=%d)", fn, B, H, Sq, Sk, D);
+  if (Hkv <= 0 || H % Hkv != 0)
+    return fail(PF_ERR_INVALID,
+                "%s: num_heads (%d) must be a multiple of num_kv_heads (%d) for grouped-query attention",
+                fn, H, Hkv);
+  if (kv_len <= 0 || kv_len > Sk)
+    return fail(PF_ERR_INVALID, "%s: kv_len must be in (0, %d], got %d", fn, Sk, kv_len);
+  if (D > 256) return fail(PF_ERR_UNSUPPORTED, "%s: head_dim %d > 256 is not built", fn, D);
+  return PF_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* pf_last_error(void) { return g_err; }
+const char* pf_version(void) { return "0.1.0+sm100a"; }
+
+int pf_device_status(int* bits_out, int reset) {
+  int v = 0;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_status(e, "pf_device_status");
+  e = cudaMemcpyFromSymbol(&v, g_status, sizeof(int));
+  if (e != cudaSuccess) return cuda_status(e, "pf_device_status");
+  if (bits_out) *bits_out = v;
+  if (reset) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_status, &zero, sizeof(int));
+    if (e != cudaSuccess) return cuda_status(e, "pf_device_status");
+  }
+  return PF_OK;
+}
+
+int pf_fwd_kernel_kind(int dtype, int head_dim) { return fwd_sm100_supported(dtype, head_dim) ? 1 : 0; }
+
+int pf_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int dtype, int B,
+           int H, int Hkv, int Sq, int Sk, int D, int causal, float sm_scale, int kv_len,
+           void* stream) {
+  int st = check_attn_shapes("pf_fwd", q, k, v, dtype, B, H, Hkv, Sq, Sk, D, kv_len);
+  if (st != PF_OK) return st;
+  if (o == nullptr) return fail(PF_ERR_INVALID, "pf_fwd: null output");
+  FwdArgs a{};
+  a.q = q; a.k = k; a.v = v; a.o = o; a.lse = lse;
+  a.dtype = dtype; a.B = B; a.H = H; a.Hkv = Hkv; a.Sq = Sq; a.Sk = Sk; a.D = D;
+  a.causal = causal != 0; a.kv_len = kv_len; a.sm_scale = sm_scale;
+  a.stream = static_cast<cudaStream_t>(stream);
+  if (fwd_sm100_supported(dtype, D) && aligned16(q) && aligned16(k) && aligned16(v) && aligned16(o))
+    return cuda_status(launch_fwd_sm100(a), "pf_fwd (tcgen05)");
+  return cuda_status(launch_fwd_simt(a), "pf_fwd (simt)");
+}
+
+int pf_rope_fwd(const void* q, const void* k, const void* v, const void* q_cos, const void* q_sin,
+                const void* k_cos, const void* k_sin, int tbl_dtype, void* o, int dtype, int B,
+                int H, int Hkv, int Sq, int Sk, int D, int causal, float sm_scale, int kv_len,
+                void* stream) {
+  int st = check_attn_shapes("pf_rope_fwd", q, k, v, dtype, B, H, Hkv, Sq, Sk, D, kv_len);
+  if (st != PF_OK) return st;
+  if (D % 2 != 0) return fail(PF_ERR_INVALID, "pf_rope_fwd: head_dim must be even for RoPE, got %d", D);
+  if (!valid_dtype(tbl_dtype)) return fail(PF_ERR_INVALID, "pf_rope_fwd: unknown table dtype %d", tbl_dtype);
+  if (!q_cos || !q_sin || !k_cos || !k_sin) return fail(PF_ERR_INVALID, "pf_rope_fwd: null rope table");
+  FwdArgs a{};
+  a.q = q; a.k = k; a.v = v; a.o = o; a.lse = nullptr;
+  a.dtype = dtype; a.B = B; a.H = H; a.Hkv = Hkv; a.Sq = Sq; a.Sk = Sk; a.D = D;
+  a.causal = causal != 0; a.kv_len = kv_len; a.sm_scale = sm_scale;
+  a.q_cos = q_cos; a.q_sin = q_sin; a.k_cos = k_cos; a.k_sin = k_sin; a.tbl_dtype = tbl_dtype;
+  a.stream = static_cast<cudaStream_t>(stream);
+  return cuda_status(launch_fwd_simt(a), "pf_rope_fwd");
+}
+
+int pf_bwd_preprocess(const void* o, const void* dout, float* delta, int dtype, int B, int H,
+                      int Sq, int D, void* stream) {
+  if (!valid_dtype(dtype) || !o || !dout || !delta) return fail(PF_ERR_INVALID, "pf_bwd_preprocess: bad argument");
+  return cuda_status(launch_bwd_preprocess(o, dout, delta, dtype, (long)B * H * Sq, D,
+                                           static_cast<cudaStream_t>(stream)),
+                     "pf_bwd_preprocess");
+}
+
+static int fill_bwd(BwdArgs* a, const char* fn, const void* q, const void* k, const void* v,
+                    const void* dout, const float* lse, const float* delta, int dtype, int B,
+                    int H, int Hkv, int Sq, int Sk, int D, int causal, float sm_scale, int kv_len,
+                    void* stream) {
+  int st = check_attn_shapes(fn, q, k, v, dtype, B, H, Hkv, Sq, Sk, D, kv_len);
+  if (st != PF_OK) return st;
+  if (!dout || !lse || !delta) return fail(PF_ERR_INVALID, "%s: null dout/lse/delta", fn);
+  *a = BwdArgs{};
+  a->q = q; a->k = k; a->v = v; a->dout = dout; a->lse = lse; a->delta = delta;
+  a->dtype = dtype; a->B = B; a->H = H; a->Hkv = Hkv; a->Sq = Sq; a->Sk = Sk; a->D = D;
+  a->causal = causal != 0; a->sm_scale = sm_scale; a->kv_len = kv_len;
+  a->stream = static_cast<cudaStream_t>(stream);
+  return PF_OK;
+}
+
+int pf_bwd_dq(const void* q, const void* k, const void* v, const void* dout, const float* lse,
+              const float* delta, void* dq, int dtype, int B, int H, int Hkv, int Sq, int Sk,
+              int D, int causal, float sm_scale, int kv_len, void* stream) {
+  BwdArgs a;
+  int st = fill_bwd(&a, "pf_bwd_dq", q, k, v, dout, lse, delta, dtype, B, H, Hkv, Sq, Sk, D,
+                    causal, sm_scale, kv_len, stream);
+  if (st != PF_OK) return st;
+  if (!dq) return fail(PF_ERR_INVALID, "pf_bwd_dq: null dq");
+  a.dq = dq;
+  return cuda_status(launch_bwd_dq_simt(a), "pf_bwd_dq");
+}
+
+int pf_bwd_dkv(const void* q, const void* k, const void* v, const void* dout, const float* lse,
+               const float* delta, void* dk, void* dv, int dtype, int B, int H, int Hkv, int Sq,
+               int Sk, int D, int causal, float sm_scale, int kv_len, void* stream) {
+  BwdArgs a;
+  int st = fill_bwd(&a, "pf_bwd_dkv", q, k, v, dout, lse, delta, dtype, B, H, Hkv, Sq, Sk, D,
+                    causal, sm_scale, kv_len, stream);
+  if (st != PF_OK) return st;
+  if (!dk || !dv) return fail(PF_ERR_INVALID, "pf_bwd_dkv: null dk/dv");
+  a.dk = dk; a.dv = dv;
+  return cuda_status(launch_bwd_dkv_simt(a), "pf_bwd_dkv");
+}
+
+size_t pf_bwd_workspace_size(int dtype, int B, int H, int Hkv, int Sq, int Sk, int D) {
+  (void)dtype; (void)Hkv; (void)Sk; (void)D;
+  const size_t delta = ((size_t)B * H * Sq * sizeof(float) + 255) / 256 * 256;
+  return delta;
+}
+
+int pf_bwd(const void* q, const void* k, const void* v, const void* o, const void* dout,
+           const float* lse, void* dq, void* dk, void* dv, int dtype, int B, int H, int Hkv,
+           int Sq, int Sk, int D, int causal, float sm_scale, int kv_len, void* workspace,
+           size_t workspace_bytes, void* stream) {
+  const size_t need = pf_bwd_workspace_size(dtype, B, H, Hkv, Sq, Sk, D);
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(PF_ERR_WORKSPACE, "pf_bwd: workspace of %zu bytes required, got %zu", need, workspace_bytes);
+  if (!o) return fail(PF_ERR_INVALID, "pf_bwd: null o");
+  float* delta = static_cast<float*>(workspace);
+  BwdArgs a;
+  int st = fill_bwd(&a, "pf_bwd", q, k, v, dout, lse, delta, dtype, B, H, Hkv, Sq, Sk, D, causal,
+                    sm_scale, kv_len, stream);
+  if (st != PF_OK) return st;
+  if (!dq || !dk || !dv) return fail(PF_ERR_INVALID, "pf_bwd: null gradient output");
+  a.dq = dq; a.dk = dk; a.dv = dv;
+  st = cuda_status(launch_bwd_preprocess(o, dout, delta, dtype, (long)B * H * Sq, D, a.stream), "pf_bwd (delta)");
+  if (st != PF_OK) return st;
+  st = cuda_status(launch_bwd_dq_simt(a), "pf_bwd (dq)");
+  if (st != PF_OK) return st;
+  return cuda_status(launch_bwd_dkv_simt(a), "pf_bwd (dkv)");
+}
+
+// ------------------------------- decode --------------------------------------
+static size_t decode_ws(int B, int H, int Hkv, int max_len, int D) {
+  int ns, sl;
+  decode_plan(max_len, B, Hkv, &ns, &sl);
+  return (size_t)B * H * ns * (D + 2) * sizeof(float);
+}
+
+size_t pf_decode_workspace_size(int B, int H, int Hkv, int C, int D) {
+  if (B <= 0 || H <= 0 || Hkv <= 0 || C <= 0 || D <= 0) return 0;
+  return decode_ws(B, H, Hkv, C, D);
+}
+
+int pf_decode(const void* q, const void* k_cache, const void* v_cache, void* o, int dtype, int B,
+              int H, int Hkv, int C, int D, int cache_len, float sm_scale, void* workspace,
+              size_t workspace_bytes, void* stream) {
+  int st = check_attn_shapes("pf_decode", q, k_cache, v_cache, dtype, B, H, Hkv, 1, C, D, cache_len);
+  if (st != PF_OK) return st;
+  if (!o) return fail(PF_ERR_INVALID, "pf_decode: null output");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (!decode_supported(D) || !aligned16(k_cache) || !aligned16(v_cache)) {
+    // Odd head sizes: the general forward kernel with one query row.
+    FwdArgs a{};
+    a.q = q; a.k = k_cache; a.v = v_cache; a.o = o; a.lse = nullptr;
+    a.dtype = dtype; a.B = B; a.H = H; a.Hkv = Hkv; a.Sq = 1; a.Sk = C; a.D = D;
+    a.causal = 0; a.kv_len = cache_len; a.sm_scale = sm_scale; a.stream = s;
+    return cuda_status(launch_fwd_simt(a), "pf_decode (simt)");
+  }
+  DecodeArgs a{};
+  a.q = q; a.k_src = k_cache; a.v_src = v_cache; a.block_tables = nullptr; a.context_lens = nullptr;
+  a.fixed_len = cache_len; a.o = o; a.dtype = dtype; a.B = B; a.H = H; a.Hkv = Hkv; a.D = D;
+  a.page_size = 1; a.cache_rows = C; a.max_len = C; a.sm_scale = sm_scale; a.stream = s;
+  decode_plan(C, B, Hkv, &a.num_splits, &a.split_len);
+  const size_t need = (size_t)B * H * a.num_splits * (D + 2) * sizeof(float);
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(PF_ERR_WORKSPACE, "pf_decode: workspace of %zu bytes required, got %zu", need, workspace_bytes);
+  a.partial = static_cast<float*>(workspace);
+  return cuda_status(launch_decode(a), "pf_decode");
+}
+
+size_t pf_paged_decode_workspace_size(int B, int H, int Hkv, int page_size, int max_context_len, int D) {
+  (void)page_size;
+  if (B <= 0 || H <= 0 || Hkv <= 0 || max_context_len <= 0 || D <= 0) return 0;
+  return decode_ws(B, H, Hkv, max_context_len, D);
+}
+
+int pf_paged_decode(const void* q, const void* k_pages, const void* v_pages,
+                    const int32_t* block_tables, const int32_t* context_lens, void* o, int dtype,
+                    int B, int H, int Hkv, int num_pages, int page_size, int pages_per_seq, int D,
+                    int max_context_len, float sm_scale, void* workspace, size_t workspace_bytes,
+                    void* stream) {
+  if (!valid_dtype(dtype)) return fail(PF_ERR_INVALID, "pf_paged_decode: unknown dtype %d", dtype);
+  if (!q || !k_pages || !v_pages || !block_tables || !context_lens || !o)
+    return fail(PF_ERR_INVALID, "pf_paged_decode: null argument");
+  if (B <= 0 || H <= 0 || D <= 0 || num_pages <= 0 || page_size <= 0 || pages_per_seq <= 0)
+    return fail(PF_ERR_INVALID, "pf_paged_decode: shapes must be positive");
+  if (Hkv <= 0 || H % Hkv != 0)
+    return fail(PF_ERR_INVALID, "pf_paged_decode: num_heads (%d) must be a multiple of num_kv_heads (%d)", H, Hkv);
+  if (!decode_supported(D))
+    return fail(PF_ERR_UNSUPPORTED, "pf_paged_decode: head_dim %d not built (64, 128, 256)", D);
+  if (!aligned16(k_pages) || !aligned16(v_pages))
+    return fail(PF_ERR_INVALID, "pf_paged_decode: page pools must be 16-byte aligned");
+  if (max_context_len <= 0) max_context_len = pages_per_seq * page_size;
+  max_context_len = max_context_len < pages_per_seq * page_size ? max_context_len : pages_per_seq * page_size;
+  DecodeArgs a{};
+  a.q = q; a.k_src = k_pages; a.v_src = v_pages; a.block_tables = block_tables;
+  a.context_lens = context_lens; a.o = o; a.dtype = dtype; a.B = B; a.H = H; a.Hkv = Hkv; a.D = D;
+  a.num_pages = num_pages; a.page_size = page_size; a.pages_per_seq = pages_per_seq;
+  a.max_len = max_context_len; a.sm_scale = sm_scale; a.stream = static_cast<cudaStream_t>(stream);
+  decode_plan(max_context_len, B, Hkv, &a.num_splits, &a.split_len);
+  const size_t need = (size_t)B * H * a.num_splits * (D + 2) * sizeof(float);
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(PF_ERR_WORKSPACE, "pf_paged_decode: workspace of %zu bytes required, got %zu", need, workspace_bytes);
+  a.partial = static_cast<float*>(workspace);
+  return cuda_status(launch_decode(a), "pf_paged_decode");
+}
+
+int pf_paged_write(void* k_pages, void* v_pages, const void* k, const void* v,
+                   const int32_t* block_tables, const int32_t* positions, int dtype, int B, int Hkv,
+                   int num_pages, int page_size, int pages_per_seq, int D, void* stream) {
+  if (!valid_dtype(dtype) || !k_pages || !v_pages || !k || !v || !block_tables || !positions)
+    return fail(PF_ERR_INVALID, "pf_paged_write: bad argument");
+  if (B <= 0 || Hkv <= 0 || num_pages <= 0 || page_size <= 0 || pages_per_seq <= 0 || D <= 0)
+    return fail(PF_ERR_INVALID, "pf_paged_write: shapes must be positive");
+  return cuda_status(launch_paged_write(k_pages, v_pages, k, v, block_tables, positions, dtype, B, Hkv,
+                                        num_pages, page_size, pages_per_seq, D,
+                                        static_cast<cudaStream_t>(stream)),
+                     "pf_paged_write");
+}
+
+int pf_cache_write(void* k_cache, void* v_cache, const void* k, const void* v, int dtype, int B,
+                   int Hkv, int C, int L, int D, int start, void* stream) {
+  if (!valid_dtype(dtype) || !k_cache || !v_cache || !k || !v)
+    return fail(PF_ERR_INVALID, "pf_cache_write: bad argument");
+  if (B <= 0 || Hkv <= 0 || C <= 0 || L < 0 || D <= 0 || start < 0)
+    return fail(PF_ERR_INVALID, "pf_cache_write: bad shape");
+  if (L > C) return fail(PF_ERR_INVALID, "pf_cache_write: %d tokens do not fit a %d-slot cache", L, C);
+  return cuda_status(launch_cache_write(k_cache, v_cache, k, v, dtype, B, Hkv, C, L, D, start,
+                                        static_cast<cudaStream_t>(stream)),
+                     "pf_cache_write");
+}
+
+int pf_paged_gather(const void* pages, const int32_t* block_tables, void* out, int dtype, int B,
+                    int Hkv, int num_pages, int page_size, int pages_per_seq, int D, void* stream) {
+  if (!valid_dtype(dtype) || !pages || !block_tables || !out)
+    return fail(PF_ERR_INVALID, "pf_paged_gather: bad argument");
+  if (B <= 0 || Hkv <= 0 || num_pages <= 0 || page_size <= 0 || pages_per_seq <= 0 || D <= 0)
+    return fail(PF_ERR_INVALID, "pf_paged_gather: shapes must be positive");
+  return cuda_status(launch_paged_gather(pages, block_tables, out, dtype, B, Hkv, num_pages, page_size,
+                                         pages_per_seq, D, static_cast<cudaStream_t>(stream)),
+                     "pf_paged_gather");
+}
+
+}  // extern "C"

@@ -1,0 +1,81 @@
+// kernels.h -- internal launch interface between the C ABI (capi.cu) and the
+// kernel translation units.  Not part of the public ABI.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stddef.h>
+
+namespace pf {
+
+struct FwdArgs {
+  const void *q, *k, *v;
+  void* o;
+  float* lse;  // may be null
+  int dtype, B, H, Hkv, Sq, Sk, D, causal, kv_len;
+  float sm_scale;
+  // fused RoPE tables (all null when RoPE is off)
+  const void *q_cos, *q_sin, *k_cos, *k_sin;
+  int tbl_dtype;
+  cudaStream_t stream;
+};
+
+struct BwdArgs {
+  const void *q, *k, *v, *dout;
+  const float *lse, *delta;
+  void *dq, *dk, *dv;
+  int dtype, B, H, Hkv, Sq, Sk, D, causal, kv_len;
+  float sm_scale;
+  float* dq_accum;  // f32 [B,H,Sq,D] scratch (tensor-core path)
+  cudaStream_t stream;
+};
+
+// Split-KV decode over a page source.  A fixed cache is described as pages of
+// `page_size` rows with an implicit identity table (block_tables == null):
+// page p of sequence b is rows [p*ps, (p+1)*ps) of cache (b, hkv).
+struct DecodeArgs {
+  const void* q;
+  const void *k_src, *v_src;
+  const int32_t* block_tables;   // null -> fixed cache
+  const int32_t* context_lens;   // null -> every sequence has `fixed_len`
+  int fixed_len;
+  void* o;
+  int dtype, B, H, Hkv, D;
+  int num_pages, page_size, pages_per_seq;  // pages: source [num_pages, Hkv, ps, D]
+  long cache_rows;                          // fixed cache capacity C
+  int max_len;                              // upper bound of the lengths
+  float sm_scale;
+  float* partial;   // workspace: [B, H, num_splits, D + 2] f32
+  int num_splits, split_len;
+  cudaStream_t stream;
+};
+
+cudaError_t launch_fwd_simt(const FwdArgs& a);
+cudaError_t launch_bwd_dq_simt(const BwdArgs& a);
+cudaError_t launch_bwd_dkv_simt(const BwdArgs& a);
+cudaError_t launch_bwd_preprocess(const void* o, const void* dout, float* delta, int dtype,
+                                  long rows, int D, cudaStream_t stream);
+
+// tcgen05 tensor-core forward (bf16/f16, D in {64, 128}).
+bool fwd_sm100_supported(int dtype, int D);
+cudaError_t launch_fwd_sm100(const FwdArgs& a);
+
+// Split-KV decode.
+void decode_plan(int max_len, int B, int Hkv, int* num_splits, int* split_len);
+bool decode_supported(int D);
+cudaError_t launch_decode(const DecodeArgs& a);
+
+cudaError_t launch_paged_write(void* k_pages, void* v_pages, const void* k, const void* v,
+                               const int32_t* block_tables, const int32_t* positions, int dtype,
+                               int B, int Hkv, int num_pages, int page_size, int pages_per_seq,
+                               int D, cudaStream_t stream);
+cudaError_t launch_cache_write(void* k_cache, void* v_cache, const void* k, const void* v,
+                               int dtype, int B, int Hkv, int C, int L, int D, int start,
+                               cudaStream_t stream);
+cudaError_t launch_paged_gather(const void* pages, const int32_t* block_tables, void* out,
+                                int dtype, int B, int Hkv, int num_pages, int page_size,
+                                int pages_per_seq, int D, cudaStream_t stream);
+
+inline int dtype_size(int dtype) { return dtype == 0 ? 4 : 2; }
+
+}  // namespace pf

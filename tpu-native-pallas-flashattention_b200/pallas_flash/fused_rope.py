@@ -1,0 +1,85 @@
+"""FlashAttention with rotary position embeddings applied inside the kernel.
+
+Drop-in for ``src/pallas_flash/fused_rope.py`` of the reference: Q and K are
+rotated (``x*cos + rotate_half(x)*sin``, fused_rope.py:43-50, :75-78) as their
+tiles are loaded, so the rotated copies never reach HBM.  Separate query and
+key tables cover decode, where the query sits at position ``pos`` and keys
+span ``[0, pos]``.  Forward only, like the reference.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+
+from . import _lib
+
+__all__ = ["flash_attention_rope"]
+
+
+def flash_attention_rope(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    q_cos: torch.Tensor,
+    q_sin: torch.Tensor,
+    k_cos: Optional[torch.Tensor] = None,
+    k_sin: Optional[torch.Tensor] = None,
+    *,
+    causal: bool = False,
+    sm_scale: Optional[float] = None,
+    block_q: int = 128,
+    block_k: int = 128,
+    kv_len: Optional[int] = None,
+    interpret: bool = False,
+) -> torch.Tensor:
+    """Attention with RoPE applied to Q and K inside the kernel.
+
+    Numerically ``flash_attention(apply_rope(q), apply_rope(k), v)`` with the
+    rotation done in fp32.  Tables are ``[seq_len_q, head_dim]`` and
+    ``[seq_len_k, head_dim]``; ``k_cos``/``k_sin`` default to the query
+    tables when the two sequence lengths agree (fused_rope.py:154-181 rules).
+    """
+    del block_q, block_k, interpret
+    if k_cos is None or k_sin is None:
+        if k.shape[2] != q.shape[2]:
+            raise ValueError(
+                "k_cos/k_sin are required when the key sequence length differs "
+                "from the query sequence length"
+            )
+        k_cos, k_sin = q_cos, q_sin
+
+    batch, num_heads, seq_len_q, head_dim = q.shape
+    num_kv_heads, seq_len_k = k.shape[1], k.shape[2]
+    if num_heads % num_kv_heads != 0:
+        raise ValueError(
+            f"num_heads ({num_heads}) must be a multiple of num_kv_heads ({num_kv_heads})"
+        )
+    if head_dim % 2 != 0:
+        raise ValueError(f"head_dim must be even for RoPE, got {head_dim}")
+    for name, tbl, want in (("q_cos", q_cos, seq_len_q), ("q_sin", q_sin, seq_len_q),
+                            ("k_cos", k_cos, seq_len_k), ("k_sin", k_sin, seq_len_k)):
+        if tuple(tbl.shape) != (want, head_dim):
+            raise ValueError(f"{name} must have shape {(want, head_dim)}, got {tuple(tbl.shape)}")
+    if k.shape != v.shape or k.shape[0] != batch or k.shape[3] != head_dim:
+        raise ValueError("k/v must be [batch, num_kv_heads, seq_len_k, head_dim] like q")
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(head_dim)
+    if kv_len is None:
+        kv_len = seq_len_k
+    elif not 0 < kv_len <= seq_len_k:
+        raise ValueError(f"kv_len must be in (0, {seq_len_k}], got {kv_len}")
+
+    _lib.require_cuda(q, k, v, q_cos, q_sin, k_cos, k_sin)
+    tdt = q_cos.dtype
+    tables = [t.to(tdt).contiguous() for t in (q_cos, q_sin, k_cos, k_sin)]
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    out = torch.empty_like(q)
+    _lib.check(_lib.lib().pf_rope_fwd(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), *(t.data_ptr() for t in tables),
+        _lib.dtype_code(tdt), out.data_ptr(), _lib.dtype_code(q.dtype), batch, num_heads,
+        num_kv_heads, seq_len_q, seq_len_k, head_dim, int(bool(causal)), float(sm_scale),
+        int(kv_len), _lib.stream_of(q)))
+    return out

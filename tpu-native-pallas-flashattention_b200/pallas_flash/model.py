@@ -1,0 +1,342 @@
+"""Tiny LLaMA decoder on the B200 attention kernels.
+
+Drop-in for ``src/pallas_flash/model.py`` of the reference: the same functions,
+parameter pytree (a dict with ``embed``, ``layers`` [list of dicts],
+``final_norm``, ``lm_head``) and greedy generation loops, on CUDA tensors.
+Attention goes through this package's kernels (``flash_attention`` for
+prefill/forward, ``flash_attention_decode`` for decode steps); the dense layers
+(projections, SwiGLU, lm_head) are plain PyTorch matmuls (cuBLAS), which the
+reference likewise leaves to its compiler.
+
+Differences that keep behaviour but suit the GPU:
+* KV caches are preallocated and written **in place** by the cache-write
+  kernel; ``decode_step`` / ``ring_decode_step`` return the same (mutated)
+  cache list, so the reference's ``logits, cache = decode_step(...)`` idiom is
+  unchanged;
+* RoPE tables are computed once per (length, dtype, device) and sliced, instead
+  of being rebuilt for ``pos + 1`` rows every step (model.py:240-243);
+* ``init_params`` takes an integer seed (or a ``torch.Generator``) where the
+  reference takes a ``jax.random.PRNGKey``.
+"""
+
+from __future__ import annotations
+
+from typing import Any, Dict, List, Optional
+
+import torch
+
+from . import _lib
+from .config import ModelConfig
+from .flash_attention import flash_attention, flash_attention_decode
+
+Params = Dict[str, Any]
+Cache = list  # per-layer list of {"k": [b, n_kv, cache_size, d], "v": same}
+
+
+# --------------------------------------------------------------------------- #
+# Building blocks (model.py:34-74)
+# --------------------------------------------------------------------------- #
+def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
+    """Root-mean-square layer norm (LLaMA-style, no mean subtraction)."""
+    xf = x.to(torch.float32)
+    var = xf.square().mean(dim=-1, keepdim=True)
+    return (xf * torch.rsqrt(var + eps) * weight).to(x.dtype)
+
+
+def precompute_rope(seq_len: int, head_dim: int, theta: float, device=None):
+    """cos/sin tables ``[seq_len, head_dim]`` (fp32): ``emb = [f, f]``, ``f = pos * theta^(-i/half)``."""
+    half = head_dim // 2
+    inv_freq = 1.0 / (theta ** (torch.arange(0, half, dtype=torch.float32, device=device) / half))
+    pos = torch.arange(seq_len, dtype=torch.float32, device=device)
+    freqs = torch.outer(pos, inv_freq)
+    emb = torch.cat([freqs, freqs], dim=-1)
+    return torch.cos(emb), torch.sin(emb)
+
+
+def _rotate_half(x: torch.Tensor) -> torch.Tensor:
+    half = x.shape[-1] // 2
+    return torch.cat([-x[..., half:], x[..., :half]], dim=-1)
+
+
+def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """Apply rotary embeddings to ``x`` ``[batch, heads, seq, head_dim]`` (tables ``[seq, head_dim]``)."""
+    return x * cos[None, None] + _rotate_half(x) * sin[None, None]
+
+
+def swiglu_mlp(x, w_gate, w_up, w_down):
+    """SwiGLU feed-forward: ``(silu(x W_gate) * (x W_up)) W_down``."""
+    return (torch.nn.functional.silu(x @ w_gate) * (x @ w_up)) @ w_down
+
+
+_ROPE_CACHE: Dict[tuple, tuple] = {}
+
+
+def _rope_slice(pos_start: int, length: int, cfg: ModelConfig, dtype, device=None):
+    """cos/sin tables for absolute positions ``[pos_start, pos_start+length)`` (model.py:240-243)."""
+    if device is None:
+        device = torch.device("cuda", torch.cuda.current_device())
+    need = pos_start + length
+    key = (cfg.head_dim, float(cfg.rope_theta), dtype, str(device))
+    ent = _ROPE_CACHE.get(key)
+    if ent is None or ent[0].shape[0] < need:
+        n = max(need, 2 * ent[0].shape[0] if ent is not None else 1024)
+        cos, sin = precompute_rope(n, cfg.head_dim, cfg.rope_theta, device=device)
+        ent = (cos.to(dtype), sin.to(dtype))
+        _ROPE_CACHE[key] = ent
+    return ent[0][pos_start:need], ent[1][pos_start:need]
+
+
+# --------------------------------------------------------------------------- #
+# Decoder block + full model (model.py:80-140)
+# --------------------------------------------------------------------------- #
+def project_qkv(params: Params, h: torch.Tensor, cfg: ModelConfig):
+    """Project normed hidden states to ``[batch, heads, seq, head_dim]`` Q, K, V (pre-RoPE)."""
+    batch, seq, _ = h.shape
+
+    def split(t, n_heads):
+        return t.reshape(batch, seq, n_heads, cfg.head_dim).transpose(1, 2)
+
+    return (split(h @ params["wq"], cfg.n_heads),
+            split(h @ params["wk"], cfg.n_kv_heads),
+            split(h @ params["wv"], cfg.n_kv_heads))
+
+
+def decoder_block(params: Params, x, cos, sin, cfg: ModelConfig, interpret: bool = False):
+    """One pre-norm transformer decoder block (causal attention on the B200 kernel)."""
+    batch, seq, _ = x.shape
+    h = rms_norm(x, params["attn_norm"], cfg.rms_norm_eps)
+    q, k, v = project_qkv(params, h, cfg)
+    q = apply_rope(q, cos, sin)
+    k = apply_rope(k, cos, sin)
+    attn = flash_attention(q, k, v, causal=True, block_q=cfg.block_q, block_k=cfg.block_k)
+    attn = attn.transpose(1, 2).reshape(batch, seq, cfg.dim)
+    x = x + attn @ params["wo"]
+    h = rms_norm(x, params["ffn_norm"], cfg.rms_norm_eps)
+    return x + swiglu_mlp(h, params["w_gate"], params["w_up"], params["w_down"])
+
+
+def forward(params: Params, tokens: torch.Tensor, cfg: ModelConfig, interpret: bool = False):
+    """Logits ``[batch, seq, vocab_size]``."""
+    seq = tokens.shape[1]
+    x = params["embed"][tokens]
+    cos, sin = _rope_slice(0, seq, cfg, x.dtype, x.device)
+    for layer in params["layers"]:
+        x = decoder_block(layer, x, cos, sin, cfg, interpret)
+    x = rms_norm(x, params["final_norm"], cfg.rms_norm_eps)
+    return x @ params["lm_head"]
+
+
+# --------------------------------------------------------------------------- #
+# Parameter initialization (model.py:146-176)
+# --------------------------------------------------------------------------- #
+def init_params(key, cfg: ModelConfig, dtype=torch.float32, device=None) -> Params:
+    """Random parameters with the reference's shapes and scales (seeded, no training)."""
+    if device is None:
+        device = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else "cpu"
+    gen = key if isinstance(key, torch.Generator) else torch.Generator().manual_seed(int(key))
+
+    def normal(shape, scale):
+        return (torch.randn(shape, generator=gen, dtype=torch.float32) * scale).to(dtype).to(device)
+
+    ones = lambda n: torch.ones((n,), dtype=dtype, device=device)  # noqa: E731
+    params: Params = {"embed": normal((cfg.vocab_size, cfg.dim), 0.02)}
+    proj = 1.0 / (cfg.dim ** 0.5)
+    layers = []
+    for _ in range(cfg.n_layers):
+        layers.append({
+            "attn_norm": ones(cfg.dim),
+            "ffn_norm": ones(cfg.dim),
+            "wq": normal((cfg.dim, cfg.dim), proj),
+            "wk": normal((cfg.dim, cfg.kv_dim), proj),
+            "wv": normal((cfg.dim, cfg.kv_dim), proj),
+            "wo": normal((cfg.dim, cfg.dim), proj),
+            "w_gate": normal((cfg.dim, cfg.ffn_hidden), proj),
+            "w_up": normal((cfg.dim, cfg.ffn_hidden), proj),
+            "w_down": normal((cfg.ffn_hidden, cfg.dim), 1.0 / (cfg.ffn_hidden ** 0.5)),
+        })
+    params["layers"] = layers
+    params["final_norm"] = ones(cfg.dim)
+    params["lm_head"] = normal((cfg.dim, cfg.vocab_size), proj)
+    return params
+
+
+def _argmax_last(logits: torch.Tensor) -> torch.Tensor:
+    return torch.argmax(logits[:, -1, :], dim=-1, keepdim=True)
+
+
+def generate(params: Params, prompt_ids, max_new_tokens: int, cfg: ModelConfig,
+             interpret: bool = False):
+    """Greedy generation by full recompute each step (model.py:182-207)."""
+    tokens = prompt_ids
+    for _ in range(max_new_tokens):
+        logits = forward(params, tokens, cfg)
+        tokens = torch.cat([tokens, _argmax_last(logits).to(tokens.dtype)], dim=1)
+    return tokens
+
+
+# --------------------------------------------------------------------------- #
+# KV-cache decoding (model.py:227-386)
+# --------------------------------------------------------------------------- #
+def _attend(layer: Params, q, k, v, cfg: ModelConfig, interpret: bool, causal: bool):
+    batch, _, seq_q, _ = q.shape
+    attn = flash_attention(q, k, v, causal=causal, block_q=cfg.block_q, block_k=cfg.block_k)
+    return attn.transpose(1, 2).reshape(batch, seq_q, cfg.dim) @ layer["wo"]
+
+
+def init_kv_cache(cfg: ModelConfig, batch: int, cache_size: int, dtype=torch.float32,
+                  device=None) -> Cache:
+    """Zeroed fixed-size KV cache for every layer."""
+    if device is None:
+        device = torch.device("cuda", torch.cuda.current_device())
+    shape = (batch, cfg.n_kv_heads, cache_size, cfg.head_dim)
+    return [{"k": torch.zeros(shape, dtype=dtype, device=device),
+             "v": torch.zeros(shape, dtype=dtype, device=device)} for _ in range(cfg.n_layers)]
+
+
+def _cache_write(layer_cache: dict, k, v, start: int) -> dict:
+    """Write ``k``/``v`` (length L) into slots ``(start + i) % C`` in place.
+
+    With ``start + L <= C`` this is the reference's ``dynamic_update_slice`` at
+    ``[start, start+L)`` (model.py:257-262); otherwise it wraps like the ring
+    slots of model.py:437-449.
+    """
+    kc, vc = layer_cache["k"], layer_cache["v"]
+    B, Hkv, C, D = kc.shape
+    L = k.shape[2]
+    kk = k.to(kc.dtype).contiguous()
+    vv = v.to(vc.dtype).contiguous()
+    _lib.check(_lib.lib().pf_cache_write(
+        kc.data_ptr(), vc.data_ptr(), kk.data_ptr(), vv.data_ptr(), _lib.dtype_code(kc.dtype),
+        B, Hkv, C, L, D, int(start), _lib.stream_of(kc)))
+    return layer_cache
+
+
+def prefill(params: Params, tokens, cfg: ModelConfig, interpret: bool = False,
+            cache_size: Optional[int] = None):
+    """Run the prompt and build the KV cache; returns ``(logits, cache)``."""
+    batch, seq = tokens.shape
+    if cache_size is None:
+        cache_size = cfg.max_seq_len
+    if cache_size < seq:
+        raise ValueError(f"cache_size ({cache_size}) must be >= prompt length ({seq})")
+    x = params["embed"][tokens]
+    cos, sin = _rope_slice(0, seq, cfg, x.dtype, x.device)
+    cache = init_kv_cache(cfg, batch, cache_size, x.dtype, x.device)
+    for idx, layer in enumerate(params["layers"]):
+        h = rms_norm(x, layer["attn_norm"], cfg.rms_norm_eps)
+        q, k, v = project_qkv(layer, h, cfg)
+        q = apply_rope(q, cos, sin)
+        k = apply_rope(k, cos, sin)
+        x = x + _attend(layer, q, k, v, cfg, interpret, causal=True)
+        _cache_write(cache[idx], k, v, 0)
+        h = rms_norm(x, layer["ffn_norm"], cfg.rms_norm_eps)
+        x = x + swiglu_mlp(h, layer["w_gate"], layer["w_up"], layer["w_down"])
+    x = rms_norm(x, params["final_norm"], cfg.rms_norm_eps)
+    return x @ params["lm_head"], cache
+
+
+def _decode_layers(params: Params, token, cache: Cache, pos: int, slot: int, kv_len: int,
+                   cfg: ModelConfig):
+    x = params["embed"][token]
+    cos, sin = _rope_slice(pos, 1, cfg, x.dtype, x.device)
+    batch = x.shape[0]
+    for layer, layer_cache in zip(params["layers"], cache):
+        h = rms_norm(x, layer["attn_norm"], cfg.rms_norm_eps)
+        q, k, v = project_qkv(layer, h, cfg)
+        q = apply_rope(q, cos, sin)
+        k = apply_rope(k, cos, sin)
+        _cache_write(layer_cache, k, v, slot)
+        attn = flash_attention_decode(q, layer_cache["k"], layer_cache["v"], kv_len,
+                                      block_k=cfg.block_k)
+        x = x + attn.transpose(1, 2).reshape(batch, 1, cfg.dim) @ layer["wo"]
+        h = rms_norm(x, layer["ffn_norm"], cfg.rms_norm_eps)
+        x = x + swiglu_mlp(h, layer["w_gate"], layer["w_up"], layer["w_down"])
+    x = rms_norm(x, params["final_norm"], cfg.rms_norm_eps)
+    return x @ params["lm_head"], cache
+
+
+def decode_step(params: Params, token, cache: Cache, pos: int, cfg: ModelConfig,
+                interpret: bool = False):
+    """Advance one token: write K/V at slot ``pos``, attend slots ``[0, pos]`` (model.py:307-356)."""
+    cache_size = cache[0]["k"].shape[2]
+    if pos >= cache_size:
+        raise ValueError(f"position {pos} exceeds cache capacity {cache_size}")
+    return _decode_layers(params, token, cache, pos, pos, pos + 1, cfg)
+
+
+def generate_cached(params: Params, prompt_ids, max_new_tokens: int, cfg: ModelConfig,
+                    interpret: bool = False, cache_size: Optional[int] = None):
+    """Greedy generation with a fixed-size KV cache (model.py:359-386).
+
+    ``cache_size`` defaults to ``prompt_len + max_new_tokens`` as in the
+    reference; a larger capacity (e.g. 512) may be given.
+    """
+    batch, prompt_len = prompt_ids.shape
+    if cache_size is None:
+        cache_size = prompt_len + max_new_tokens
+    logits, cache = prefill(params, prompt_ids, cfg, cache_size=cache_size)
+    next_tok = _argmax_last(logits).to(prompt_ids.dtype)
+    out = [prompt_ids, next_tok]
+    for i in range(max_new_tokens - 1):
+        logits, cache = decode_step(params, next_tok, cache, prompt_len + i, cfg)
+        next_tok = _argmax_last(logits).to(prompt_ids.dtype)
+        out.append(next_tok)
+    return torch.cat(out, dim=1)
+
+
+# --------------------------------------------------------------------------- #
+# Ring-buffer cache (model.py:389-531)
+# --------------------------------------------------------------------------- #
+def init_ring_cache(cfg: ModelConfig, batch: int, capacity: int, dtype=torch.float32,
+                    device=None) -> Cache:
+    """Ring-buffer KV cache holding the most recent ``capacity`` tokens."""
+    return init_kv_cache(cfg, batch, capacity, dtype, device)
+
+
+def ring_kv_len(total_tokens: int, capacity: int) -> int:
+    """Number of live slots after ``total_tokens`` have been written."""
+    return min(total_tokens, capacity)
+
+
+def prefill_ring(params: Params, tokens, cfg: ModelConfig, capacity: int,
+                 interpret: bool = False):
+    """Prefill into a ring cache keeping the last ``capacity`` tokens at slots ``pos % capacity``."""
+    batch, seq = tokens.shape
+    x = params["embed"][tokens]
+    cos, sin = _rope_slice(0, seq, cfg, x.dtype, x.device)
+    keep = min(seq, capacity)
+    start = seq - keep
+    cache = init_ring_cache(cfg, batch, capacity, x.dtype, x.device)
+    for idx, layer in enumerate(params["layers"]):
+        h = rms_norm(x, layer["attn_norm"], cfg.rms_norm_eps)
+        q, k, v = project_qkv(layer, h, cfg)
+        q = apply_rope(q, cos, sin)
+        k = apply_rope(k, cos, sin)
+        x = x + _attend(layer, q, k, v, cfg, interpret, causal=True)
+        _cache_write(cache[idx], k[:, :, start:], v[:, :, start:], start)
+        h = rms_norm(x, layer["ffn_norm"], cfg.rms_norm_eps)
+        x = x + swiglu_mlp(h, layer["w_gate"], layer["w_up"], layer["w_down"])
+    x = rms_norm(x, params["final_norm"], cfg.rms_norm_eps)
+    return x @ params["lm_head"], cache
+
+
+def ring_decode_step(params: Params, token, cache: Cache, pos: int, cfg: ModelConfig,
+                     interpret: bool = False):
+    """One decode step against a ring cache: write slot ``pos % C``, attend the live window."""
+    capacity = cache[0]["k"].shape[2]
+    return _decode_layers(params, token, cache, pos, pos % capacity,
+                          ring_kv_len(pos + 1, capacity), cfg)
+
+
+def generate_streaming(params: Params, prompt_ids, max_new_tokens: int, cfg: ModelConfig,
+                       window: int, interpret: bool = False):
+    """Greedy generation in constant memory with a ring-buffer cache of ``window`` slots."""
+    batch, prompt_len = prompt_ids.shape
+    logits, cache = prefill_ring(params, prompt_ids, cfg, window)
+    next_tok = _argmax_last(logits).to(prompt_ids.dtype)
+    out: List[torch.Tensor] = [prompt_ids, next_tok]
+    for i in range(max_new_tokens - 1):
+        logits, cache = ring_decode_step(params, next_tok, cache, prompt_len + i, cfg)
+        next_tok = _argmax_last(logits).to(prompt_ids.dtype)
+        out.append(next_tok)
+    return torch.cat(out, dim=1)

@@ -1,0 +1,165 @@
+"""Paged attention (block-table KV cache) on B200.
+
+Drop-in for ``src/pallas_flash/paged.py`` of the reference.  Layout:
+
+    k_pages / v_pages : [num_pages, num_kv_heads, page_size, head_dim]
+    block_tables      : [batch, pages_per_seq]  int32  (logical -> physical page)
+    context_lens      : [batch]                 int32  (valid tokens per sequence)
+
+The decode kernel resolves ``block_tables[b, p]`` on the device while it
+streams pages into shared memory with bulk copies; pages at or past
+``context_lens[b]`` are never read (so, unlike the reference, unused trailing
+table entries need not be valid page ids).  One CTA serves all query heads of
+a kv head, so each page crosses HBM once per step.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+
+from . import _lib
+
+__all__ = ["paged_flash_attention", "init_paged_cache", "write_to_paged_cache",
+           "write_to_paged_cache_batch", "gather_paged"]
+
+
+def paged_flash_attention(
+    q: torch.Tensor,
+    k_pages: torch.Tensor,
+    v_pages: torch.Tensor,
+    block_tables: torch.Tensor,
+    context_lens: torch.Tensor,
+    *,
+    sm_scale: Optional[float] = None,
+    interpret: bool = False,
+    max_context_len: Optional[int] = None,
+) -> torch.Tensor:
+    """Single-query attention over a paged KV cache (paged.py:102-192).
+
+    Returns ``[batch, num_heads, 1, head_dim]``.  ``max_context_len`` is an
+    optional upper bound of ``context_lens`` (it sizes the split grid; the
+    default is the table capacity ``pages_per_seq * page_size``).
+    """
+    del interpret
+    if q.ndim != 4 or q.shape[2] != 1:
+        raise ValueError(
+            f"paged attention expects q of shape [batch, heads, 1, head_dim], got {tuple(q.shape)}"
+        )
+    if k_pages.shape != v_pages.shape:
+        raise ValueError("k_pages and v_pages must have the same shape")
+    batch, num_heads, _, head_dim = q.shape
+    num_pages, num_kv_heads, page_size, k_head_dim = k_pages.shape
+    if k_head_dim != head_dim:
+        raise ValueError("q and pages must share head_dim")
+    if num_heads % num_kv_heads != 0:
+        raise ValueError(
+            f"num_heads ({num_heads}) must be a multiple of num_kv_heads ({num_kv_heads})"
+        )
+    if block_tables.ndim != 2 or block_tables.shape[0] != batch:
+        raise ValueError(
+            f"block_tables must be [batch, pages_per_seq], got {tuple(block_tables.shape)}"
+        )
+    if tuple(context_lens.shape) != (batch,):
+        raise ValueError(f"context_lens must be [batch], got {tuple(context_lens.shape)}")
+    if not (q.dtype == k_pages.dtype == v_pages.dtype):
+        raise ValueError("q and the page pools must share a dtype")
+    _lib.require_cuda(q, k_pages, v_pages)
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(head_dim)
+    dev = q.device
+    tables = block_tables.to(device=dev, dtype=torch.int32).contiguous()
+    lens = context_lens.to(device=dev, dtype=torch.int32).contiguous()
+    pages_per_seq = tables.shape[1]
+    cap = pages_per_seq * page_size
+    max_len = cap if max_context_len is None else max(1, min(int(max_context_len), cap))
+    q, k_pages, v_pages = q.contiguous(), k_pages.contiguous(), v_pages.contiguous()
+    out = torch.empty_like(q)
+    L = _lib.lib()
+    ws = _lib.workspace(
+        L.pf_paged_decode_workspace_size(batch, num_heads, num_kv_heads, page_size, max_len, head_dim), dev)
+    _lib.check(L.pf_paged_decode(
+        q.data_ptr(), k_pages.data_ptr(), v_pages.data_ptr(), tables.data_ptr(), lens.data_ptr(),
+        out.data_ptr(), _lib.dtype_code(q.dtype), batch, num_heads, num_kv_heads, num_pages,
+        page_size, pages_per_seq, head_dim, max_len, float(sm_scale), ws.data_ptr(), ws.numel(),
+        _lib.stream_of(q)))
+    return out
+
+
+def init_paged_cache(num_pages: int, num_kv_heads: int, page_size: int, head_dim: int,
+                     dtype=torch.float32, device=None):
+    """Allocate an empty (zeroed) page pool ``(k_pages, v_pages)`` (paged.py:198-202)."""
+    if device is None:
+        device = torch.device("cuda", torch.cuda.current_device())
+    shape = (num_pages, num_kv_heads, page_size, head_dim)
+    return (torch.zeros(shape, dtype=dtype, device=device),
+            torch.zeros(shape, dtype=dtype, device=device))
+
+
+def write_to_paged_cache_batch(k_pages, v_pages, k, v, block_tables, positions):
+    """Writes one token per sequence, in place.
+
+    ``k``/``v``: ``[batch, num_kv_heads, 1, head_dim]``; ``block_tables``:
+    ``[batch, pages_per_seq]``; ``positions``: ``[batch]`` absolute positions.
+    Token b lands in page ``block_tables[b, pos // page_size]`` at offset
+    ``pos % page_size``.  Returns ``(k_pages, v_pages)``.
+    """
+    _lib.require_cuda(k_pages, v_pages, k, v)
+    num_pages, n_kv, page_size, head_dim = k_pages.shape
+    batch = k.shape[0]
+    if k.shape != (batch, n_kv, 1, head_dim) or v.shape != k.shape:
+        raise ValueError(f"k/v must be [batch, {n_kv}, 1, {head_dim}], got {tuple(k.shape)}")
+    if not (k_pages.is_contiguous() and v_pages.is_contiguous()):
+        raise ValueError("page pools must be contiguous to be written in place")
+    dev = k_pages.device
+    tables = torch.as_tensor(block_tables, dtype=torch.int32, device=dev).reshape(batch, -1).contiguous()
+    pos = torch.as_tensor(positions, dtype=torch.int32, device=dev).reshape(batch).contiguous()
+    kk = k.to(k_pages.dtype).contiguous()
+    vv = v.to(v_pages.dtype).contiguous()
+    _lib.check(_lib.lib().pf_paged_write(
+        k_pages.data_ptr(), v_pages.data_ptr(), kk.data_ptr(), vv.data_ptr(), tables.data_ptr(),
+        pos.data_ptr(), _lib.dtype_code(k_pages.dtype), batch, n_kv, num_pages, page_size,
+        tables.shape[1], head_dim, _lib.stream_of(k_pages)))
+    return k_pages, v_pages
+
+
+def write_to_paged_cache(k_pages, v_pages, k, v, block_table, position: int):
+    """Write one token's K/V into the page holding ``position`` (paged.py:205-223).
+
+    ``k``/``v``: ``[1, num_kv_heads, 1, head_dim]``; ``block_table``:
+    ``[pages_per_seq]``.  The pools are updated in place and returned, so the
+    reference's functional ``k_pages, v_pages = write_to_paged_cache(...)``
+    idiom works unchanged.  A physical page id outside the pool is clamped
+    (``dynamic_update_slice`` semantics); a logical page beyond the table
+    raises ``IndexError`` like indexing a jax array with a static int.
+    """
+    page_size = k_pages.shape[2]
+    logical_page = int(position) // page_size
+    n_entries = int(block_table.shape[0]) if hasattr(block_table, "shape") else len(block_table)
+    if not 0 <= logical_page < n_entries:
+        raise IndexError(
+            f"index {logical_page} is out of bounds for axis 0 with size {n_entries}")
+    return write_to_paged_cache_batch(k_pages, v_pages, k, v,
+                                      torch.as_tensor(block_table).reshape(1, -1),
+                                      [int(position)])
+
+
+def gather_paged(pages: torch.Tensor, block_tables: torch.Tensor) -> torch.Tensor:
+    """Contiguous ``[batch, num_kv_heads, pages_per_seq*page_size, head_dim]`` view of a pool.
+
+    Byte-exact materialisation of the block-table index map
+    (``(block_tables[b, p], h, :, :)``, paged.py:158-159); out-of-range page
+    ids are flagged in the device status word instead of being read.
+    """
+    _lib.require_cuda(pages)
+    num_pages, n_kv, page_size, head_dim = pages.shape
+    tables = block_tables.to(device=pages.device, dtype=torch.int32).contiguous()
+    batch, pps = tables.shape
+    out = torch.empty((batch, n_kv, pps * page_size, head_dim), dtype=pages.dtype, device=pages.device)
+    _lib.check(_lib.lib().pf_paged_gather(
+        pages.contiguous().data_ptr(), tables.data_ptr(), out.data_ptr(),
+        _lib.dtype_code(pages.dtype), batch, n_kv, num_pages, page_size, pps, head_dim,
+        _lib.stream_of(pages)))
+    return out
