@@ -93,3 +93,55 @@ def test_golden_grads_on_gpu(golden):
         (out * to_dev(c["do"])).sum().backward()
         for t, n in ((tq, "dq"), (tk, "dk"), (tv, "dv")):
             assert rel_err(to_np(t.grad), c[n]) < 1e-4, (name, n)
+
+
+# ---------------------------------------------------------------- tensor-core path
+TC_CASES = [
+    # (B, H, Hkv, Sq, Sk, D, causal, kv_len)
+    (1, 2, 2, 128, 128, 128, True, None),
+    (2, 4, 2, 256, 256, 128, False, None),
+    (1, 4, 1, 200, 200, 128, True, None),
+    (1, 8, 2, 1000, 1000, 64, True, None),
+    (2, 4, 4, 64, 64, 64, False, None),
+    (1, 4, 2, 300, 700, 128, True, None),
+    (1, 4, 2, 90, 640, 128, False, 333),
+    (1, 2, 1, 257, 257, 64, True, 130),
+]
+
+
+@pytest.mark.parametrize("case", TC_CASES)
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_tensor_core_grads(case, dtype):
+    B, H, Hkv, Sq, Sk, D, causal, kv_len = case
+    q, k, v = randn((B, H, Sq, D), 21), randn((B, Hkv, Sk, D), 22), randn((B, Hkv, Sk, D), 23)
+    cot = randn((B, H, Sq, D), 24)
+    tq, tk, tv = (to_dev(x, dtype).requires_grad_(True) for x in (q, k, v))
+    out = pf.flash_attention(tq, tk, tv, causal=causal, kv_len=kv_len)
+    out.backward(to_dev(cot, dtype))
+    want = orc.attention_vjp(widen(tq), widen(tk), widen(tv), widen(to_dev(cot, dtype)), causal=causal,
+                             kv_len=kv_len)
+    for t, w, name in zip((tq, tk, tv), want, ("dq", "dk", "dv")):
+        assert t.grad.dtype == dtype
+        g = to_np(t.grad)
+        assert np.all(np.isfinite(g)), name
+        assert rel_err(g, w) < 2e-2, (name, rel_err(g, w))
+    if kv_len is not None:
+        assert float(tk.grad[:, :, kv_len:].float().abs().max()) == 0.0
+
+
+def test_tensor_core_grads_c2_shape_sampled():
+    """Config 2 shape at reduced batch (B1 H32 Hkv8 S4096 D128, causal): a few (head, row) slices."""
+    g = torch.Generator(device="cuda").manual_seed(7)
+    shp_q, shp_k = (1, 32, 4096, 128), (1, 8, 4096, 128)
+    tq = torch.randn(shp_q, device="cuda", generator=g).to(torch.bfloat16).requires_grad_(True)
+    tk = torch.randn(shp_k, device="cuda", generator=g).to(torch.bfloat16).requires_grad_(True)
+    tv = torch.randn(shp_k, device="cuda", generator=g).to(torch.bfloat16).requires_grad_(True)
+    do = torch.randn(shp_q, device="cuda", generator=g).to(torch.bfloat16)
+    pf.flash_attention(tq, tk, tv, causal=True).backward(do)
+    # kv head 3 (q heads 12..15), full-precision oracle on that group only
+    sl = slice(12, 16)
+    want = orc.attention_vjp(widen(tq[:, sl]), widen(tk[:, 3:4]), widen(tv[:, 3:4]), widen(do[:, sl]),
+                             causal=True, dtype=np.float32)
+    for t, w, name in ((tq.grad[:, sl], want[0], "dq"), (tk.grad[:, 3:4], want[1], "dk"),
+                       (tv.grad[:, 3:4], want[2], "dv")):
+        assert rel_err(to_np(t), w) < 2e-2, name

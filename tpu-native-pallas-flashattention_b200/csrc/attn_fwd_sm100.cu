@@ -29,6 +29,7 @@
 #include <type_traits>
 #include "common.cuh"
 #include "kernels.h"
+#include "sm100_util.cuh"
 
 namespace pf {
 namespace {
@@ -59,21 +60,6 @@ struct Bars {
   uint64_t s_full[2], p_full[2], o_done[2];
   uint32_t tmem_base;
 };
-
-// Descriptor for a K-major 128 x D tile stored as kBoxes swizzled boxes of
-// 128 rows x 128 B; k-step kk covers elements [16 kk, 16 kk + 16).
-template <int D>
-__device__ __forceinline__ uint64_t desc_kmajor(uint32_t tile_addr, int kk) {
-  const uint32_t addr = tile_addr + (kk >> 2) * (kBM * 128) + (kk & 3) * 32;
-  return smem_desc_sw128(addr, 16, 1024);
-}
-// Descriptor for V (B operand of P.V, MN-major): rows = keys, columns = d.
-// k-step kk covers keys [16 kk, 16 kk + 16) = 2 groups of 8 rows (SBO apart);
-// the next 64 columns live in the next box (LBO apart).
-template <int D>
-__device__ __forceinline__ uint64_t desc_v(uint32_t tile_addr, int kk) {
-  return smem_desc_sw128(tile_addr + kk * 16 * 128, kBN * 128, 1024);
-}
 
 template <typename T, int D>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -178,7 +164,7 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         const uint32_t k_addr = sbase + Cfg::kKOff + (j % NS) * Cfg::kTileBytes;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk)
-          umma_ss(tmem + s_col[w], desc_kmajor<D>(q_addr[w], kk), desc_kmajor<D>(k_addr, kk),
+          umma_ss(tmem + s_col[w], desc_k<kBM>(q_addr[w], kk), desc_k<kBN>(k_addr, kk),
                   idesc_qk, kk > 0 ? 1u : 0u);
         umma_commit(&bars->s_full[w]);
       };
@@ -186,7 +172,7 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         const uint32_t v_addr = sbase + Cfg::kVOff + (j % NS) * Cfg::kTileBytes;
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk)
-          umma_ts(tmem + o_col[w], tmem + s_col[w] + kk * 8, desc_v<D>(v_addr, kk), idesc_pv,
+          umma_ts(tmem + o_col[w], tmem + s_col[w] + kk * 8, desc_mn<kBN>(v_addr, kk), idesc_pv,
                   (j > 0 || kk > 0) ? 1u : 0u);
         umma_commit(&bars->o_done[w]);
       };
@@ -339,50 +325,13 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   }
 }
 
-// --------------------------------------------------------------------------
-// Host side: tensor maps through the driver entry point (no -lcuda needed).
-// --------------------------------------------------------------------------
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn get_encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  if (fn == nullptr) {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-  }
-  return fn;
-}
-
-// 3-D map over a [planes, rows_stride, D] tensor that exposes `rows` rows per
-// plane; box = 64 columns x 128 rows, 128-byte swizzle, zero fill past `rows`.
-bool make_map(CUtensorMap* m, const void* base, int dtype, int D, int rows, long row_stride_rows,
-              int planes) {
-  EncodeTiledFn enc = get_encode_fn();
-  if (enc == nullptr) return false;
-  const CUtensorMapDataType dt =
-      dtype == PF_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)rows, (cuuint64_t)planes};
-  cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)row_stride_rows * D * 2};
-  cuuint32_t box[3] = {64, 128, 1};
-  cuuint32_t estr[3] = {1, 1, 1};
-  return enc(m, dt, 3, const_cast<void*>(base), dims, strides, box, estr,
-             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 template <typename T, int D>
 cudaError_t launch_t(const FwdArgs& a) {
   using Cfg = FwdCfg<D>;
   CUtensorMap tq, tk, tv;
-  if (!make_map(&tq, a.q, a.dtype, D, a.Sq, a.Sq, a.B * a.H) ||
-      !make_map(&tk, a.k, a.dtype, D, a.kv_len, a.Sk, a.B * a.Hkv) ||
-      !make_map(&tv, a.v, a.dtype, D, a.kv_len, a.Sk, a.B * a.Hkv))
+  if (!make_tile_map(&tq, a.q, a.dtype, D, a.Sq, a.Sq, a.B * a.H, kBM) ||
+      !make_tile_map(&tk, a.k, a.dtype, D, a.kv_len, a.Sk, a.B * a.Hkv, kBN) ||
+      !make_tile_map(&tv, a.v, a.dtype, D, a.kv_len, a.Sk, a.B * a.Hkv, kBN))
     return cudaErrorInvalidValue;
   auto kern = fwd_sm100_kernel<T, D>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);

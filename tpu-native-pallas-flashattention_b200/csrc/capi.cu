@@ -117,6 +117,13 @@ int pf_bwd_preprocess(const void* o, const void* dout, float* delta, int dtype, 
                      "pf_bwd_preprocess");
 }
 
+// Tensor-core backward: 16-bit inputs, head_dim 64/128, 16-byte aligned operands.
+static bool use_tc_bwd(const BwdArgs& a) {
+  return bwd_sm100_supported(a.dtype, a.D) && aligned16(a.q) && aligned16(a.k) && aligned16(a.v) &&
+         aligned16(a.dout) && (a.dq == nullptr || aligned16(a.dq)) && (a.dk == nullptr || aligned16(a.dk)) &&
+         (a.dv == nullptr || aligned16(a.dv));
+}
+
 static int fill_bwd(BwdArgs* a, const char* fn, const void* q, const void* k, const void* v,
                     const void* dout, const float* lse, const float* delta, int dtype, int B,
                     int H, int Hkv, int Sq, int Sk, int D, int causal, float sm_scale, int kv_len,
@@ -141,6 +148,7 @@ int pf_bwd_dq(const void* q, const void* k, const void* v, const void* dout, con
   if (st != PF_OK) return st;
   if (!dq) return fail(PF_ERR_INVALID, "pf_bwd_dq: null dq");
   a.dq = dq;
+  if (use_tc_bwd(a)) return cuda_status(launch_bwd_dq_sm100(a), "pf_bwd_dq (tcgen05)");
   return cuda_status(launch_bwd_dq_simt(a), "pf_bwd_dq");
 }
 
@@ -153,6 +161,7 @@ int pf_bwd_dkv(const void* q, const void* k, const void* v, const void* dout, co
   if (st != PF_OK) return st;
   if (!dk || !dv) return fail(PF_ERR_INVALID, "pf_bwd_dkv: null dk/dv");
   a.dk = dk; a.dv = dv;
+  if (use_tc_bwd(a)) return cuda_status(launch_bwd_dkv_sm100(a), "pf_bwd_dkv (tcgen05)");
   return cuda_status(launch_bwd_dkv_simt(a), "pf_bwd_dkv");
 }
 
@@ -179,6 +188,11 @@ int pf_bwd(const void* q, const void* k, const void* v, const void* o, const voi
   a.dq = dq; a.dk = dk; a.dv = dv;
   st = cuda_status(launch_bwd_preprocess(o, dout, delta, dtype, (long)B * H * Sq, D, a.stream), "pf_bwd (delta)");
   if (st != PF_OK) return st;
+  if (use_tc_bwd(a)) {
+    st = cuda_status(launch_bwd_dkv_sm100(a), "pf_bwd (dkv, tcgen05)");
+    if (st != PF_OK) return st;
+    return cuda_status(launch_bwd_dq_sm100(a), "pf_bwd (dq, tcgen05)");
+  }
   st = cuda_status(launch_bwd_dq_simt(a), "pf_bwd (dq)");
   if (st != PF_OK) return st;
   return cuda_status(launch_bwd_dkv_simt(a), "pf_bwd (dkv)");

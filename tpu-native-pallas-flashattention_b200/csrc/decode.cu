@@ -43,7 +43,6 @@ struct DecodeCfg {
   static constexpr int kNPL = D / 32;             // output dims per lane
 };
 
-template <typename T> struct Vec;  // NPL elements of T as one load
 template <int N, typename T> __device__ __forceinline__ void load_row_part(const T* p, float (&out)[N]) {
 #pragma unroll
   for (int i = 0; i < N; ++i) out[i] = to_f(p[i]);
@@ -281,8 +280,7 @@ cudaError_t launch_decode_t(const DecodeArgs& a) {
   kern<<<grid, Cfg::kWarps * 32, smem, a.stream>>>(a, head_chunks);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  decode_combine_kernel<T><<<a.B * a.H, D < 128 ? D : 128, 0, a.stream>>>(a);
-  return cudaGetLastError();
+  return launch_decode_combine(a);
 }
 
 template <typename T, int D>
@@ -380,7 +378,20 @@ void decode_plan(int max_len, int B, int Hkv, int* num_splits, int* split_len) {
   *num_splits = (max_len + sl - 1) / sl;
 }
 
+cudaError_t launch_decode_combine(const DecodeArgs& a) {
+  const int th = a.D < 128 ? a.D : 128;
+  switch (a.dtype) {
+    case PF_F32: decode_combine_kernel<float><<<a.B * a.H, th, 0, a.stream>>>(a); break;
+    case PF_BF16: decode_combine_kernel<__nv_bfloat16><<<a.B * a.H, th, 0, a.stream>>>(a); break;
+    default: decode_combine_kernel<__half><<<a.B * a.H, th, 0, a.stream>>>(a);
+  }
+  return cudaGetLastError();
+}
+
 cudaError_t launch_decode(const DecodeArgs& a) {
+  const bool paged = a.block_tables != nullptr;
+  const long rows = paged ? (long)a.num_pages * a.Hkv * a.page_size : 0;
+  if (decode_tc_supported(a.dtype, a.D, a.page_size, paged, rows)) return launch_decode_tc(a);
   switch (a.dtype) {
     case PF_F32: return launch_decode_d<float>(a);
     case PF_BF16: return launch_decode_d<__nv_bfloat16>(a);

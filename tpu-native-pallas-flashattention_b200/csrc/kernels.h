@@ -60,10 +60,19 @@ cudaError_t launch_bwd_preprocess(const void* o, const void* dout, float* delta,
 bool fwd_sm100_supported(int dtype, int D);
 cudaError_t launch_fwd_sm100(const FwdArgs& a);
 
+// tcgen05 tensor-core backward (same dtypes / head dims as the forward).
+bool bwd_sm100_supported(int dtype, int D);
+cudaError_t launch_bwd_dkv_sm100(const BwdArgs& a);
+cudaError_t launch_bwd_dq_sm100(const BwdArgs& a);
+
 // Split-KV decode.
 void decode_plan(int max_len, int B, int Hkv, int* num_splits, int* split_len);
 bool decode_supported(int D);
 cudaError_t launch_decode(const DecodeArgs& a);
+cudaError_t launch_decode_combine(const DecodeArgs& a);
+// Tensor-core decode (bf16/f16, D 64/128); launch_decode dispatches to it.
+bool decode_tc_supported(int dtype, int D, int page_size, bool paged, long rows);
+cudaError_t launch_decode_tc(const DecodeArgs& a);
 
 cudaError_t launch_paged_write(void* k_pages, void* v_pages, const void* k, const void* v,
                                const int32_t* block_tables, const int32_t* positions, int dtype,

@@ -1,0 +1,43 @@
+// sm100_util.cuh -- host and device helpers shared by the tcgen05 kernels:
+// TMA tensor maps over [planes, rows, D] 16-bit tensors and the UMMA shared-
+// memory descriptors of the tiles those maps produce.
+//
+// Every tile is stored as D/64 "boxes" of `rows` x 64 elements (128-byte rows,
+// 128-byte swizzle, 1024-byte swizzle atoms of 8 rows).  One physical layout
+// serves two operand roles:
+//   K-major  (rows = M or N, contiguous 64-element chunks along K = d):
+//            k-step kk (16 elements) starts 32*(kk%4) bytes into box kk/4;
+//   MN-major (rows = K, contiguous chunks along N = d):
+//            k-step kk (16 rows) starts 16*128*kk bytes in; the next 64
+//            columns are one box further (LBO), 8-row groups 1024 B apart (SBO).
+#pragma once
+
+#include <cuda.h>
+#include "common.cuh"
+
+namespace pf {
+
+template <int ROWS>
+__device__ __forceinline__ uint64_t desc_k(uint32_t tile_addr, int kk) {
+  const uint32_t addr = tile_addr + (kk >> 2) * (ROWS * 128) + (kk & 3) * 32;
+  return smem_desc_sw128(addr, 16, 1024);
+}
+
+template <int ROWS>
+__device__ __forceinline__ uint64_t desc_mn(uint32_t tile_addr, int kk) {
+  return smem_desc_sw128(tile_addr + kk * 16 * 128, ROWS * 128, 1024);
+}
+
+// TMEM column of k-step kk of a 16-bit operand that two warpgroups packed
+// into their own 32-column halves (q or key columns [32w, 32w + 32) -> packed
+// columns [32w, 32w + 16)) of a 64-column buffer.
+__device__ __forceinline__ uint32_t split_packed_col(int kk) {
+  return (uint32_t)((kk >> 1) * 32 + (kk & 1) * 8);
+}
+
+// 16-bit [planes, row_stride_rows, D] tensor exposing `rows` rows per plane,
+// box = 64 columns x box_rows rows, 128-byte swizzle, zero fill past `rows`.
+bool make_tile_map(CUtensorMap* m, const void* base, int dtype, int D, int rows,
+                   long row_stride_rows, int planes, int box_rows);
+
+}  // namespace pf
