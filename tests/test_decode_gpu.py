@@ -100,3 +100,24 @@ def test_decode_step_rejects_overflow():
     _, cache = pf.prefill(params, torch.tensor([[1, 2]], device="cuda"), cfg, cache_size=4)
     with pytest.raises(ValueError):
         pf.decode_step(params, torch.tensor([[3]], device="cuda"), cache, 4, cfg)
+
+
+@pytest.mark.parametrize("G", [1, 3, 16, 32])
+def test_decode_head_groups_bf16(G):
+    """Query-head groups from MHA to 32 q heads per kv head (head chunks of 16 on the tensor-core path)."""
+    B, Hkv, C, D = 2, 2, 300, 128
+    q, k, v = randn((B, G * Hkv, 1, D), 7), randn((B, Hkv, C, D), 8), randn((B, Hkv, C, D), 9)
+    tq, tk, tv = (to_dev(x, torch.bfloat16) for x in (q, k, v))
+    out = pf.flash_attention_decode(tq, tk, tv, 257)
+    ref = orc.reference_attention(widen(tq), widen(tk)[:, :, :257], widen(tv)[:, :, :257])
+    assert np.max(np.abs(to_np(out) - ref)) < 2e-2
+
+
+def test_decode_nan_tail_bf16():
+    filled = 37
+    k = torch.cat([torch.ones((2, 2, filled, 64)), torch.full((2, 2, 91, 64), float("nan"))], dim=2)
+    k = k.to(torch.bfloat16).cuda()
+    q = torch.ones((2, 8, 1, 64), dtype=torch.bfloat16, device="cuda")
+    out = pf.flash_attention_decode(q, k, k, filled)
+    assert torch.isfinite(out.float()).all()
+    assert torch.allclose(out.float(), torch.ones_like(out, dtype=torch.float32), atol=1e-5)
