@@ -146,6 +146,23 @@ int pf_paged_decode(const void* q, const void* k_pages, const void* v_pages,
                     int max_context_len, float sm_scale, void* workspace,
                     size_t workspace_bytes, void* stream);
 
+/* Paged decode without a caller workspace.  No counterpart in the reference:
+ * it exists for callers that cannot allocate device memory (a host that
+ * manages device memory as fixed arenas, or a call site handed only its
+ * input and output buffers, where cudaMalloc -- which also synchronises the
+ * device -- is not allowed).  Same arguments and results as pf_paged_decode;
+ * the split-KV scratch is a fixed 16 MiB __device__ array inside the library
+ * (held by every GPU that loads it until exit).  The first call on a device
+ * resolves that array's address; make it before any stream capture.  Calls
+ * that overlap on the GPU race on the shared scratch.  Requests needing more
+ * than 16 MiB of partials even at one split per sequence (B*H*(D+2)*4 bytes)
+ * return PF_ERR_WORKSPACE. */
+int pf_paged_decode_noalloc(const void* q, const void* k_pages, const void* v_pages,
+                            const int32_t* block_tables, const int32_t* context_lens,
+                            void* o, int dtype, int B, int H, int Hkv, int num_pages,
+                            int page_size, int pages_per_seq, int D,
+                            int max_context_len, float sm_scale, void* stream);
+
 /* ---------------------------------------------------------------------------
  * Cache bookkeeping.
  * pf_paged_write: for each sequence b of the batch, write one token's k/v

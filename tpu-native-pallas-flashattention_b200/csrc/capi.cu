@@ -53,6 +53,16 @@ int check_attn_shapes(const char* fn, const void* q, const void* k, const void* 
 
 }  // namespace
 
+namespace pf {
+int set_last_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+}  // namespace pf
+
 extern "C" {
 
 const char* pf_last_error(void) { return g_err; }

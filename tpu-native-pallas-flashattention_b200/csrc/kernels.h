@@ -85,6 +85,9 @@ cudaError_t launch_paged_gather(const void* pages, const int32_t* block_tables, 
                                 int dtype, int B, int Hkv, int num_pages, int page_size,
                                 int pages_per_seq, int D, cudaStream_t stream);
 
+// Records the message returned by pf_last_error() and returns `code`.
+int set_last_error(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+
 inline int dtype_size(int dtype) { return dtype == 0 ? 4 : 2; }
 
 }  // namespace pf

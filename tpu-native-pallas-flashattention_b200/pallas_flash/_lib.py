@@ -54,6 +54,7 @@ _SIGNATURES = {
     "pf_decode": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _F, _P, _Z, _P]),
     "pf_paged_decode_workspace_size": (_Z, [_I, _I, _I, _I, _I, _I]),
     "pf_paged_decode": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _F, _P, _Z, _P]),
+    "pf_paged_decode_noalloc": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _F, _P]),
     "pf_paged_write": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P]),
     "pf_cache_write": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P]),
     "pf_paged_gather": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P]),
