@@ -80,14 +80,19 @@ int pf_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
            int dtype, int B, int H, int Hkv, int Sq, int Sk, int D,
            int causal, float sm_scale, int kv_len, void* stream);
 
-/* Forward with RoPE fused in: q and k are rotated inside the kernel with
- * x*cos + rotate_half(x)*sin, q by rows of (q_cos, q_sin) [Sq, D] and k by
- * rows of (k_cos, k_sin) [Sk, D] (table dtype tbl_dtype).  No lse output. */
+/* Forward with RoPE fused in: q and k are rotated with x*cos +
+ * rotate_half(x)*sin, q by rows of (q_cos, q_sin) [Sq, D] and k by rows of
+ * (k_cos, k_sin) [Sk, D] (table dtype tbl_dtype).  No lse output.  On the
+ * tensor-core path each query tile is rotated once in shared memory and each
+ * key row once into the workspace (pf_rope_fwd_workspace_size bytes; 0 for
+ * the fp32 path, which rotates both operands as it loads them). */
+size_t pf_rope_fwd_workspace_size(int dtype, int B, int Hkv, int Sk, int D);
 int pf_rope_fwd(const void* q, const void* k, const void* v,
                 const void* q_cos, const void* q_sin,
                 const void* k_cos, const void* k_sin, int tbl_dtype,
                 void* o, int dtype, int B, int H, int Hkv, int Sq, int Sk,
-                int D, int causal, float sm_scale, int kv_len, void* stream);
+                int D, int causal, float sm_scale, int kv_len,
+                void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Backward.  delta [B,H,Sq] f32 = sum_d o*do.

@@ -60,7 +60,7 @@ def test_rejects_bad_dtype_and_big_head_dim():
 
 def test_rope_rejects_odd_head_dim():
     lib = _lib.load_library()
-    st = lib.pf_rope_fwd(256, 256, 256, 256, 256, 256, 256, 0, 256, 0, 1, 2, 2, 4, 4, 5, 0, 0.1, 4, None)
+    st = lib.pf_rope_fwd(256, 256, 256, 256, 256, 256, 256, 0, 256, 0, 1, 2, 2, 4, 4, 5, 0, 0.1, 4, None, 0, None)
     assert st == _lib.PF_ERR_INVALID
     assert "even" in lib.pf_last_error().decode()
 

@@ -84,3 +84,44 @@ def test_fused_requires_k_tables_when_lengths_differ():
     cos, sin = tables(1)
     with pytest.raises(ValueError):
         pf.flash_attention_rope(q, k, k, cos, sin, block_q=1)
+
+
+@pytest.mark.parametrize("H,Hkv,Sq,Sk,D,causal,kv_len", [
+    (4, 2, 256, 256, 128, True, None),
+    (4, 1, 200, 200, 128, False, None),
+    (8, 2, 130, 130, 64, True, None),
+    (2, 2, 1, 256, 128, False, 38),     # decode shape: query at position 37, separate tables
+    (4, 2, 300, 700, 64, True, 650),
+])
+@pytest.mark.parametrize("tdt", [torch.float32, torch.bfloat16])
+def test_fused_tensor_core_path(H, Hkv, Sq, Sk, D, causal, kv_len, tdt):
+    q, k, v = randn((2, H, Sq, D), 40), randn((2, Hkv, Sk, D), 41), randn((2, Hkv, Sk, D), 42)
+    cos, sin = tables(max(Sq, Sk), D)
+    pos0 = 37 if Sq == 1 else 0
+    qc, qs = cos[pos0:pos0 + Sq].to(tdt), sin[pos0:pos0 + Sq].to(tdt)
+    kc, ks = cos[:Sk].to(tdt), sin[:Sk].to(tdt)
+    tq, tk, tv = (to_dev(x, torch.bfloat16) for x in (q, k, v))
+    out = pf.flash_attention_rope(tq, tk, tv, qc, qs, kc, ks, causal=causal, kv_len=kv_len)
+    f = lambda t: t.float().cpu().numpy()  # noqa: E731
+    ref = orc.reference_attention(orc.apply_rope(widen(tq), f(qc), f(qs)), orc.apply_rope(widen(tk), f(kc), f(ks)),
+                                  widen(tv), causal=causal, kv_len=kv_len)
+    assert np.max(np.abs(to_np(out) - ref)) < 2e-2
+
+
+def test_c3_shape_sampled():
+    """Config 3 shape at batch 1 (H32 Hkv8 S8192 D128, causal, bf16): head 5's output vs fp32 oracle."""
+    g = torch.Generator(device="cuda").manual_seed(3)
+    S = 8192
+    tq = torch.randn((1, 32, S, 128), device="cuda", generator=g).to(torch.bfloat16)
+    tk = torch.randn((1, 8, S, 128), device="cuda", generator=g).to(torch.bfloat16)
+    tv = torch.randn((1, 8, S, 128), device="cuda", generator=g).to(torch.bfloat16)
+    cos, sin = tables(S)
+    out = pf.flash_attention_rope(tq, tk, tv, cos, sin, causal=True)
+    c, s = cos.cpu().numpy(), sin.cpu().numpy()
+    rows = np.array([0, 1, 4095, 8191])
+    qrot = orc.apply_rope(widen(tq[:, 5:6]), c, s)[:, :, rows]
+    krot = orc.apply_rope(widen(tk[:, 1:2]), c, s)
+    vv = widen(tv[:, 1:2])
+    for i, r in enumerate(rows):
+        ref = orc.reference_attention(qrot[:, :, i:i + 1], krot[:, :, :r + 1], vv[:, :, :r + 1], dtype=np.float32)
+        assert np.max(np.abs(to_np(out[:, 5:6, r:r + 1]) - ref)) < 2e-2, r

@@ -56,17 +56,46 @@ struct FwdCfg {
 
 struct Bars {
   uint64_t q;
+  uint64_t q_ready[2];  // RoPE: query tile w rotated in shared memory
   uint64_t k_full[4], v_full[4], kv_empty[4];
   uint64_t s_full[2], p_full[2], o_done[2];
   uint32_t tmem_base;
 };
 
+// Rotates one query row of a swizzled 128 x D tile in place:
+// x*cos + rotate_half(x)*sin with table row `pos` (fused_rope.py:43-50, :75-78).
 template <typename T, int D>
+__device__ __forceinline__ void rope_row_in_smem(uint8_t* tile, int row, const void* cos_t, const void* sin_t,
+                                                 int tbl_dtype, long pos) {
+  constexpr int half = D / 2;
+#pragma unroll 1
+  for (int d0 = 0; d0 < half; d0 += 8) {
+    const int d1 = d0 + half;
+    uint4* p0 = reinterpret_cast<uint4*>(tile + (d0 >> 6) * (kBM * 128) + row * 128 + ((((d0 & 63) >> 3) ^ (row & 7)) << 4));
+    uint4* p1 = reinterpret_cast<uint4*>(tile + (d1 >> 6) * (kBM * 128) + row * 128 + ((((d1 & 63) >> 3) ^ (row & 7)) << 4));
+    uint4 v0 = *p0, v1 = *p1;
+    T* x0 = reinterpret_cast<T*>(&v0);
+    T* x1 = reinterpret_cast<T*>(&v1);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const float a = to_f(x0[u]), bb = to_f(x1[u]);
+      const long i0 = pos * D + d0 + u, i1 = pos * D + d1 + u;
+      const float r0 = a * load_any(cos_t, tbl_dtype, i0) - bb * load_any(sin_t, tbl_dtype, i0);
+      const float r1 = bb * load_any(cos_t, tbl_dtype, i1) + a * load_any(sin_t, tbl_dtype, i1);
+      x0[u] = from_f<T>(r0);
+      x1[u] = from_f<T>(r1);
+    }
+    *p0 = v0;
+    *p1 = v1;
+  }
+}
+
+template <typename T, int D, bool ROPE>
 __global__ void __launch_bounds__(kThreads, 1)
 fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                  const __grid_constant__ CUtensorMap tm_v, T* __restrict__ out,
                  float* __restrict__ lse, int B, int H, int Hkv, int Sq, int kv_len, int causal,
-                 float scale_log2, int n_qtiles) {
+                 float scale_log2, int n_qtiles, const void* q_cos, const void* q_sin, int tbl_dtype) {
   using Cfg = FwdCfg<D>;
   constexpr int NS = Cfg::kStages;
   constexpr int fmt = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
@@ -103,6 +132,8 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->q, 1);
+    mbar_init(&bars->q_ready[0], kBM);
+    mbar_init(&bars->q_ready[1], kBM);
     for (int s = 0; s < NS; ++s) {
       mbar_init(&bars->k_full[s], 1);
       mbar_init(&bars->v_full[s], 1);
@@ -155,7 +186,13 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   } else if (warp == 1) {
     // ------------------------------ MMA issuer ----------------------------
     if (lane == 0 && n_max > 0) {
-      bool ok = mbar_wait(&bars->q, 0);
+      bool ok = true;
+      if (ROPE) {
+        for (int w = 0; w < 2; ++w)
+          if (n_w[w] > 0) ok = ok && mbar_wait(&bars->q_ready[w], 0);
+      } else {
+        ok = mbar_wait(&bars->q, 0);
+      }
       tc_fence_after();
       const uint32_t q_addr[2] = {sbase + Cfg::kQOff, sbase + Cfg::kQOff + Cfg::kTileBytes};
       const uint32_t s_col[2] = {Cfg::kS0, Cfg::kS1};
@@ -215,7 +252,15 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     const uint32_t o_addr = lane_base + (w == 0 ? Cfg::kO0 : Cfg::kO1);
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
-    for (int j = 0; j < n; ++j) {
+    if (ROPE && n > 0) {
+      // Rotate this warpgroup's query tile once, before any S MMA reads it.
+      ok = mbar_wait(&bars->q, 0);
+      if (ok && qpos < Sq)
+        rope_row_in_smem<T, D>(smem + Cfg::kQOff + w * Cfg::kTileBytes, row, q_cos, q_sin, tbl_dtype, qpos);
+      fence_proxy_async_smem();  // generic-proxy writes -> tensor-core (async proxy) reads
+      mbar_arrive(&bars->q_ready[w]);
+    }
+    for (int j = 0; ok && j < n; ++j) {
       if (!mbar_wait(&bars->s_full[w], j & 1)) { ok = false; break; }
       tc_fence_after();
       const int k0 = j * kBN;
@@ -325,23 +370,68 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   }
 }
 
-template <typename T, int D>
-cudaError_t launch_t(const FwdArgs& a) {
+template <typename T, int D, bool ROPE>
+cudaError_t launch_t(const FwdArgs& a, const void* k_rot) {
   using Cfg = FwdCfg<D>;
   CUtensorMap tq, tk, tv;
   if (!make_tile_map(&tq, a.q, a.dtype, D, a.Sq, a.Sq, a.B * a.H, kBM) ||
-      !make_tile_map(&tk, a.k, a.dtype, D, a.kv_len, a.Sk, a.B * a.Hkv, kBN) ||
+      !make_tile_map(&tk, ROPE ? k_rot : a.k, a.dtype, D, a.kv_len, a.Sk, a.B * a.Hkv, kBN) ||
       !make_tile_map(&tv, a.v, a.dtype, D, a.kv_len, a.Sk, a.B * a.Hkv, kBN))
     return cudaErrorInvalidValue;
-  auto kern = fwd_sm100_kernel<T, D>;
+  auto kern = fwd_sm100_kernel<T, D, ROPE>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
   if (e != cudaSuccess) return e;
   const int n_qtiles = (a.Sq + 2 * kBM - 1) / (2 * kBM);
   dim3 grid((unsigned)(n_qtiles * a.B * a.H));
   const float scale_log2 = a.sm_scale * kLog2e;
   kern<<<grid, kThreads, Cfg::kSmem, a.stream>>>(tq, tk, tv, (T*)a.o, a.lse, a.B, a.H, a.Hkv, a.Sq,
-                                                 a.kv_len, a.causal, scale_log2, n_qtiles);
+                                                 a.kv_len, a.causal, scale_log2, n_qtiles, a.q_cos, a.q_sin,
+                                                 a.tbl_dtype);
   return cudaGetLastError();
+}
+
+
+// K rotated once per row into `out` ([B*Hkv, Sk, D], rows < kv_len), so the
+// attention kernel streams pre-rotated keys: each key row is rotated once
+// instead of once per (query head, query tile) that reads it.
+template <typename T, int D>
+__global__ void rope_rows_kernel(const T* __restrict__ x, T* __restrict__ out, const void* cos_t,
+                                 const void* sin_t, int tbl_dtype, int Sk, int kv_len, long n_items) {
+  constexpr int half = D / 2, per_row = half / 8;
+  for (long it = (long)blockIdx.x * blockDim.x + threadIdx.x; it < n_items; it += (long)gridDim.x * blockDim.x) {
+    const long row = it / per_row;            // over planes * kv_len
+    const int d0 = (int)(it % per_row) * 8, d1 = d0 + half;
+    const long plane = row / kv_len;
+    const int pos = (int)(row % kv_len);
+    const long base = (plane * Sk + pos) * D;
+    uint4 v0 = *reinterpret_cast<const uint4*>(x + base + d0);
+    uint4 v1 = *reinterpret_cast<const uint4*>(x + base + d1);
+    T* x0 = reinterpret_cast<T*>(&v0);
+    T* x1 = reinterpret_cast<T*>(&v1);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const float a = to_f(x0[u]), bb = to_f(x1[u]);
+      const long i0 = (long)pos * D + d0 + u, i1 = (long)pos * D + d1 + u;
+      const float r0 = a * load_any(cos_t, tbl_dtype, i0) - bb * load_any(sin_t, tbl_dtype, i0);
+      const float r1 = bb * load_any(cos_t, tbl_dtype, i1) + a * load_any(sin_t, tbl_dtype, i1);
+      x0[u] = from_f<T>(r0);
+      x1[u] = from_f<T>(r1);
+    }
+    *reinterpret_cast<uint4*>(out + base + d0) = v0;
+    *reinterpret_cast<uint4*>(out + base + d1) = v1;
+  }
+}
+
+template <typename T, int D>
+cudaError_t launch_rope_t(const FwdArgs& a, void* k_rot) {
+  const long n_items = (long)a.B * a.Hkv * a.kv_len * (D / 16);
+  const int threads = 256;
+  const long blocks = (n_items + threads - 1) / threads;
+  rope_rows_kernel<T, D><<<(unsigned)(blocks < 148L * 32 ? blocks : 148L * 32), threads, 0, a.stream>>>(
+      (const T*)a.k, (T*)k_rot, a.k_cos, a.k_sin, a.tbl_dtype, a.Sk, a.kv_len, n_items);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  return launch_t<T, D, true>(a, k_rot);
 }
 
 }  // namespace
@@ -351,8 +441,20 @@ bool fwd_sm100_supported(int dtype, int D) {
 }
 
 cudaError_t launch_fwd_sm100(const FwdArgs& a) {
-  if (a.dtype == PF_BF16) return a.D == 128 ? launch_t<__nv_bfloat16, 128>(a) : launch_t<__nv_bfloat16, 64>(a);
-  return a.D == 128 ? launch_t<__half, 128>(a) : launch_t<__half, 64>(a);
+  if (a.dtype == PF_BF16)
+    return a.D == 128 ? launch_t<__nv_bfloat16, 128, false>(a, nullptr) : launch_t<__nv_bfloat16, 64, false>(a, nullptr);
+  return a.D == 128 ? launch_t<__half, 128, false>(a, nullptr) : launch_t<__half, 64, false>(a, nullptr);
+}
+
+size_t rope_fwd_sm100_workspace(int dtype, int B, int Hkv, int Sk, int D) {
+  (void)dtype;
+  return ((size_t)B * Hkv * Sk * D * 2 + 255) / 256 * 256;
+}
+
+cudaError_t launch_rope_fwd_sm100(const FwdArgs& a, void* k_rot) {
+  if (a.dtype == PF_BF16)
+    return a.D == 128 ? launch_rope_t<__nv_bfloat16, 128>(a, k_rot) : launch_rope_t<__nv_bfloat16, 64>(a, k_rot);
+  return a.D == 128 ? launch_rope_t<__half, 128>(a, k_rot) : launch_rope_t<__half, 64>(a, k_rot);
 }
 
 }  // namespace pf

@@ -101,22 +101,34 @@ int pf_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int
   return cuda_status(launch_fwd_simt(a), "pf_fwd (simt)");
 }
 
+size_t pf_rope_fwd_workspace_size(int dtype, int B, int Hkv, int Sk, int D) {
+  if (!fwd_sm100_supported(dtype, D) || B <= 0 || Hkv <= 0 || Sk <= 0) return 0;
+  return rope_fwd_sm100_workspace(dtype, B, Hkv, Sk, D);
+}
+
 int pf_rope_fwd(const void* q, const void* k, const void* v, const void* q_cos, const void* q_sin,
                 const void* k_cos, const void* k_sin, int tbl_dtype, void* o, int dtype, int B,
                 int H, int Hkv, int Sq, int Sk, int D, int causal, float sm_scale, int kv_len,
-                void* stream) {
+                void* workspace, size_t workspace_bytes, void* stream) {
   int st = check_attn_shapes("pf_rope_fwd", q, k, v, dtype, B, H, Hkv, Sq, Sk, D, kv_len);
   if (st != PF_OK) return st;
   if (D % 2 != 0) return fail(PF_ERR_INVALID, "pf_rope_fwd: head_dim must be even for RoPE, got %d", D);
   if (!valid_dtype(tbl_dtype)) return fail(PF_ERR_INVALID, "pf_rope_fwd: unknown table dtype %d", tbl_dtype);
   if (!q_cos || !q_sin || !k_cos || !k_sin) return fail(PF_ERR_INVALID, "pf_rope_fwd: null rope table");
+  if (o == nullptr) return fail(PF_ERR_INVALID, "pf_rope_fwd: null output");
   FwdArgs a{};
   a.q = q; a.k = k; a.v = v; a.o = o; a.lse = nullptr;
   a.dtype = dtype; a.B = B; a.H = H; a.Hkv = Hkv; a.Sq = Sq; a.Sk = Sk; a.D = D;
   a.causal = causal != 0; a.kv_len = kv_len; a.sm_scale = sm_scale;
   a.q_cos = q_cos; a.q_sin = q_sin; a.k_cos = k_cos; a.k_sin = k_sin; a.tbl_dtype = tbl_dtype;
   a.stream = static_cast<cudaStream_t>(stream);
-  return cuda_status(launch_fwd_simt(a), "pf_rope_fwd");
+  if (fwd_sm100_supported(dtype, D) && aligned16(q) && aligned16(k) && aligned16(v) && aligned16(o)) {
+    const size_t need = rope_fwd_sm100_workspace(dtype, B, Hkv, Sk, D);
+    if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))
+      return fail(PF_ERR_WORKSPACE, "pf_rope_fwd: workspace of %zu bytes required, got %zu", need, workspace_bytes);
+    return cuda_status(launch_rope_fwd_sm100(a, workspace), "pf_rope_fwd (tcgen05)");
+  }
+  return cuda_status(launch_fwd_simt(a), "pf_rope_fwd (simt)");
 }
 
 int pf_bwd_preprocess(const void* o, const void* dout, float* delta, int dtype, int B, int H,

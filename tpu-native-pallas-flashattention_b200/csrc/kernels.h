@@ -59,6 +59,10 @@ cudaError_t launch_bwd_preprocess(const void* o, const void* dout, float* delta,
 // tcgen05 tensor-core forward (bf16/f16, D in {64, 128}).
 bool fwd_sm100_supported(int dtype, int D);
 cudaError_t launch_fwd_sm100(const FwdArgs& a);
+// Fused-RoPE forward: Q rotated in shared memory, K rotated once per row into
+// k_rot (rope_fwd_sm100_workspace bytes) and streamed from there.
+size_t rope_fwd_sm100_workspace(int dtype, int B, int Hkv, int Sk, int D);
+cudaError_t launch_rope_fwd_sm100(const FwdArgs& a, void* k_rot);
 
 // tcgen05 tensor-core backward (same dtypes / head dims as the forward).
 bool bwd_sm100_supported(int dtype, int D);

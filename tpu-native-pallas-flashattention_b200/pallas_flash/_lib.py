@@ -44,7 +44,8 @@ _SIGNATURES = {
     "pf_device_status": (_I, [ctypes.POINTER(_I), _I]),
     "pf_fwd_kernel_kind": (_I, [_I, _I]),
     "pf_fwd": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _F, _I, _P]),
-    "pf_rope_fwd": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _P, _I, _I, _I, _I, _I, _I, _I, _I, _F, _I, _P]),
+    "pf_rope_fwd_workspace_size": (_Z, [_I, _I, _I, _I, _I]),
+    "pf_rope_fwd": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _P, _I, _I, _I, _I, _I, _I, _I, _I, _F, _I, _P, _Z, _P]),
     "pf_bwd_preprocess": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _P]),
     "pf_bwd_dq": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _F, _I, _P]),
     "pf_bwd_dkv": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _F, _I, _P]),

@@ -1,8 +1,11 @@
 """FlashAttention with rotary position embeddings applied inside the kernel.
 
 Drop-in for ``src/pallas_flash/fused_rope.py`` of the reference: Q and K are
-rotated (``x*cos + rotate_half(x)*sin``, fused_rope.py:43-50, :75-78) as their
-tiles are loaded, so the rotated copies never reach HBM.  Separate query and
+rotated with ``x*cos + rotate_half(x)*sin`` (fused_rope.py:43-50, :75-78).
+On the tensor-core path each query tile is rotated once in shared memory (the
+rotated Q never reaches HBM) and each key row is rotated exactly once into a
+workspace that the attention kernel streams -- the reference instead rotates
+the K block for every (query head, query block) that reads it.  Separate query and
 key tables cover decode, where the query sits at position ``pos`` and keys
 span ``[0, pos]``.  Forward only, like the reference.
 """
@@ -77,9 +80,13 @@ def flash_attention_rope(
     tables = [t.to(tdt).contiguous() for t in (q_cos, q_sin, k_cos, k_sin)]
     q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
     out = torch.empty_like(q)
-    _lib.check(_lib.lib().pf_rope_fwd(
+    L = _lib.lib()
+    code = _lib.dtype_code(q.dtype)
+    ws = _lib.workspace(L.pf_rope_fwd_workspace_size(code, batch, num_kv_heads, seq_len_k, head_dim),
+                        q.device)
+    _lib.check(L.pf_rope_fwd(
         q.data_ptr(), k.data_ptr(), v.data_ptr(), *(t.data_ptr() for t in tables),
-        _lib.dtype_code(tdt), out.data_ptr(), _lib.dtype_code(q.dtype), batch, num_heads,
+        _lib.dtype_code(tdt), out.data_ptr(), code, batch, num_heads,
         num_kv_heads, seq_len_q, seq_len_k, head_dim, int(bool(causal)), float(sm_scale),
-        int(kv_len), _lib.stream_of(q)))
+        int(kv_len), ws.data_ptr(), ws.numel(), _lib.stream_of(q)))
     return out
