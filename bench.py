@@ -182,10 +182,10 @@ def time_kernels(pf, q, k, v, do, iters=5):
     return fwd_ms / iters, bwd_ms / iters
 
 
-def paged_decode_bench(pf, dev, iters=10):
+def paged_decode_bench(pf, dev, iters=10, n_seqs=256, warmup=3):
     """Config 4: paged decode HBM GB/s (bytes = 4096 B per live token + q/out + table)."""
     rng = np.random.default_rng(0)
-    nb, hq, hkv, ps, d = 256, 32, 8, 16, 128
+    nb, hq, hkv, ps, d = n_seqs, 32, 8, 16, 128
     lens = rng.integers(512, 32769, size=nb)
     npages = [(int(x) + ps - 1) // ps for x in lens]
     pool = int(math.ceil(1.1 * sum(npages)))
@@ -202,7 +202,7 @@ def paged_decode_bench(pf, dev, iters=10):
     q = torch.randn((nb, hq, 1, d), device=dev, generator=g).to(torch.bfloat16)
     tt = torch.from_numpy(table).to(dev)
     ll = torch.from_numpy(lens.astype(np.int32)).to(dev)
-    for _ in range(3):
+    for _ in range(warmup):
         pf.paged_flash_attention(q, kp, vp, tt, ll, max_context_len=32768)
     torch.cuda.synchronize()
     s = torch.cuda.current_stream()
@@ -217,8 +217,80 @@ def paged_decode_bench(pf, dev, iters=10):
     nbytes = tokens * hkv * d * 2 * 2 + 2 * nb * hq * d * 2 + 4 * sum(npages)
     del kp, vp
     torch.cuda.empty_cache()
-    return {"workload": "config 4: 256 seqs, kv_len U[512,32768] (seed 0), page 16, H32/Hkv8/D128, bf16",
+    return {"workload": f"config 4: {nb} seqs, kv_len U[512,32768] (seed 0), page 16, H32/Hkv8/D128, bf16",
             "tokens": tokens, "bytes": nbytes, "ms": ms, "GB/s": nbytes / ms / 1e6}
+
+
+def fixed_decode_bench(pf, dev, iters=5):
+    """Config 4 fixed-cache variant: cache [256, 8, 32768, 128] bf16, cache_len 32768 (HBM GB/s)."""
+    nb, hq, hkv, c, d = 256, 32, 8, 32768, 128
+    g = torch.Generator(device=dev).manual_seed(1)
+    kc = torch.empty((nb, hkv, c, d), device=dev, dtype=torch.bfloat16).normal_(generator=g)
+    vc = torch.empty((nb, hkv, c, d), device=dev, dtype=torch.bfloat16).normal_(generator=g)
+    q = torch.randn((nb, hq, 1, d), device=dev, generator=g).to(torch.bfloat16)
+    for _ in range(2):
+        pf.flash_attention_decode(q, kc, vc, c)
+    torch.cuda.synchronize()
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(iters):
+        pf.flash_attention_decode(q, kc, vc, c)
+    e1.record(s)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / iters
+    nbytes = nb * hkv * c * d * 2 * 2 + 2 * nb * hq * d * 2
+    del kc, vc
+    torch.cuda.empty_cache()
+    return {"workload": "config 4 fixed cache: [256, 8, 32768, 128] bf16, cache_len 32768",
+            "bytes": nbytes, "ms": ms, "GB/s": nbytes / ms / 1e6}
+
+
+def rope_prefill_bench(pf, dev, iters=5):
+    """Config 3: fused-RoPE prefill B8 H32 Hkv8 S8192 D128 causal bf16 (TFLOP/s, 4.398e12 FLOP)."""
+    b, h, hkv, s_, d = 8, 32, 8, 8192, 128
+    g = torch.Generator(device=dev).manual_seed(2)
+    q = torch.randn((b, h, s_, d), device=dev, generator=g).to(torch.bfloat16)
+    k = torch.randn((b, hkv, s_, d), device=dev, generator=g).to(torch.bfloat16)
+    v = torch.randn((b, hkv, s_, d), device=dev, generator=g).to(torch.bfloat16)
+    cos, sin = pf.precompute_rope(s_, d, 10000.0, device=dev)
+    for _ in range(2):
+        pf.flash_attention_rope(q, k, v, cos, sin, causal=True)
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(iters):
+        pf.flash_attention_rope(q, k, v, cos, sin, causal=True)
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / iters
+    flop = 4.0 * b * h * s_ * s_ * d / 2
+    return {"workload": "config 3: fused-RoPE prefill B8 H32 Hkv8 S8192 D128 causal bf16 (theta 1e4)",
+            "flop": flop, "ms": ms, "TFLOP/s": flop / ms / 1e9}
+
+
+def generation_bench(pf, dev):
+    """Config 5: tiny-LLaMA greedy generation tokens/s (generate_cached, then ring streaming)."""
+    cfg = pf.ModelConfig(vocab_size=32000, dim=512, n_layers=8, n_heads=8, n_kv_heads=2, head_dim=64,
+                         ffn_hidden=1408, rope_theta=10000.0, rms_norm_eps=1e-5)
+    params = pf.init_params(0, cfg, dtype=torch.bfloat16, device=dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+    prompts = torch.randint(0, 32000, (16, 128), device=dev, generator=g)
+    pf.generate_cached(params, prompts, 8, cfg, cache_size=512)
+    pf.generate_streaming(params, prompts, 8, cfg, window=512)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    pf.generate_cached(params, prompts, 256, cfg, cache_size=512)
+    torch.cuda.synchronize()
+    t1 = time.perf_counter()
+    pf.generate_streaming(params, prompts, 4096, cfg, window=512)
+    torch.cuda.synchronize()
+    t2 = time.perf_counter()
+    return {"workload": "config 5: tiny LLaMA (dim 512, 8 layers, 8/2 heads, head_dim 64, bf16), batch 16, prompt 128",
+            "cached_tokens_per_s": 16 * 256 / (t1 - t0), "cached_s": t1 - t0,
+            "streaming_tokens_per_s": 16 * 4096 / (t2 - t1), "streaming_s": t2 - t1,
+            "timing": "wall clock around the host loop, synchronised before and after"}
 
 
 def e2e_step(pf, host_in, host_out, dev):
@@ -235,7 +307,9 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--no-extras", action="store_true", help="skip paged decode and CPU baseline")
+    ap.add_argument("--no-extras", action="store_true", help="skip the secondary workloads and CPU baseline")
+    ap.add_argument("--mode", choices=["bench", "profile-c2", "profile-decode"], default="bench",
+                    help="profile-*: only launch the kernels of one workload (for ncu captures)")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -274,7 +348,20 @@ def main():
     torch.cuda.set_device(dev)
     _lib.load_library()
 
+    if args.mode == "profile-decode":
+        # config-4 shape on 32 sequences (~2.4 GB of KV): warmup + steps decode calls
+        paged_decode_bench(pf, dev, iters=args.steps, n_seqs=32, warmup=args.warmup)
+        torch.cuda.synchronize()
+        print(json.dumps({"mode": args.mode, "ok": True}))
+        return
     q, k, v, do = make_inputs(dev, seed=rank)
+    if args.mode == "profile-c2":
+        # warmup + steps fwd+bwd steps of config 2 and nothing else
+        for _ in range(args.warmup + args.steps):
+            step_device(pf, q, k, v, do)
+        torch.cuda.synchronize()
+        print(json.dumps({"mode": args.mode, "ok": True}))
+        return
     for _ in range(max(3, args.warmup)):
         step_device(pf, q, k, v, do)
     torch.cuda.synchronize()
@@ -352,6 +439,13 @@ def main():
         pd["frac_of_hbm"] = pd["GB/s"] / hbm
         pd["hbm_peak_gbs"] = hbm
         line["paged_decode"] = pd
+        fd = fixed_decode_bench(pf, dev)
+        fd["frac_of_hbm"] = fd["GB/s"] / hbm
+        line["fixed_decode"] = fd
+        rp = rope_prefill_bench(pf, dev)
+        rp["frac_of_bf16_peak"] = rp["TFLOP/s"] / tf_burst
+        line["rope_prefill"] = rp
+        line["generation"] = generation_bench(pf, dev)
         line["cpu_baseline"] = cpu_baseline(steps=1)
     if rank == 0:
         print(json.dumps(line))

@@ -196,3 +196,26 @@ def test_c4_shape_sampled():
         vc = pf.gather_paged(vp, to_dev(table[b:b + 1]))[:, :, :lens[b]]
         ref = orc.reference_attention(widen(q[b:b + 1]), widen(kc), widen(vc), dtype=np.float32)
         assert np.max(np.abs(to_np(out[b:b + 1]) - ref)) < 2e-2
+
+
+def test_sequence_sharding_is_bitwise_identical():
+    """Each rank's local pool + remapped table gives the same bits as the full problem."""
+    from pallas_flash import sharding
+    rng = np.random.default_rng(2)
+    B, H, Hkv, ps, D = 12, 8, 2, 16, 128
+    lens = rng.integers(1, 2000, size=B)
+    pps = int(lens.max()) // ps + 1
+    num_pages = B * pps
+    table = scrambled_table(B, pps, num_pages, 5)
+    g = torch.Generator(device="cuda").manual_seed(6)
+    kp = torch.randn((num_pages, Hkv, ps, D), device="cuda", generator=g).to(torch.bfloat16)
+    vp = torch.randn((num_pages, Hkv, ps, D), device="cuda", generator=g).to(torch.bfloat16)
+    q = torch.randn((B, H, 1, D), device="cuda", generator=g).to(torch.bfloat16)
+    tt, ll = to_dev(table), torch.tensor(lens, dtype=torch.int32, device="cuda")
+    cap = pps * ps
+    full = pf.paged_flash_attention(q, kp, vp, tt, ll, max_context_len=cap)
+    for seqs in sharding.greedy_balance(lens, 3):
+        ql, kl, vl, tl, lt = sharding.local_paged_problem(q, kp, vp, tt, ll, seqs)
+        tl = torch.nn.functional.pad(tl, (0, pps - tl.shape[1]))
+        part = pf.paged_flash_attention(ql, kl, vl, tl, lt, max_context_len=cap)
+        assert torch.equal(part, full[seqs]), seqs

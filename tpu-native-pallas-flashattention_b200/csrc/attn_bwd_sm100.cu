@@ -45,36 +45,42 @@ struct BwdCfg {
   static constexpr int kStreamTile = 64 * D * 2;  // 64-row streamed tile
   static constexpr int kFixedOff = 0;             // two resident tiles
   static constexpr int kStreamOff = 2 * kFixedTile;
-  static constexpr int kBarOff = kStreamOff + kNS * 2 * kStreamTile;
+  static constexpr int kStatOff = kStreamOff + kNS * 2 * kStreamTile;  // [kNS][64] float2 (-lse2, -delta)
+  static constexpr int kBarOff = kStatOff + kNS * 64 * 8;
   static constexpr int kSmem = kBarOff + 256 + 1024;
   static constexpr uint32_t kS = 0, kDP = 128, kAcc = 256;
   static constexpr uint32_t kTmemCols = 512;
 };
 
 // Elementwise step shared by both kernels.  Thread owns TMEM lane `row`; its
-// 32 columns [32w, 32w + 32) of S/dP buffer b become P and dS.  visible(c)
-// says whether column c (0..31 of this thread's half) is unmasked; lse2 /
-// delta give the column's or the row's statistics.
-template <int FMT, typename Vis, typename Lse, typename Dlt>
-__device__ __forceinline__ void p_ds_step(uint32_t s_addr, uint32_t dp_addr, float scale_log2,
-                                          Vis visible, Lse lse2, Dlt delta) {
+// 32 columns [32w, 32w + 32) of S/dP buffer b become P and dS, packed to
+// 16-bit pairs over the first 16 of those columns.  `full` (warp-uniform)
+// means every column is visible; otherwise visible(c) decides.  nl2(c) is
+// -lse*log2(e) and nd(c) is -delta for column c (or the thread's row).
+template <int FMT, typename Vis, typename NL2, typename ND>
+__device__ __forceinline__ void p_ds_step(uint32_t s_addr, uint32_t dp_addr, float scale_log2, bool full,
+                                          Vis visible, NL2 nl2, ND nd) {
   uint32_t rs[32], rd[32];
   tmem_ld32(s_addr, rs);
   tmem_ld32(dp_addr, rd);
   tmem_wait_ld();
   uint32_t pp[16], pd[16];
+  const float2 sc2 = make_float2(scale_log2, scale_log2);
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
-    float p[2], ds[2];
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const int c = 2 * i + u;
-      const float pv = visible(c) ? fast_exp2(fmaf(__uint_as_float(rs[c]), scale_log2, -lse2(c))) : 0.f;
-      p[u] = pv;
-      ds[u] = pv * (__uint_as_float(rd[c]) - delta(c));
+    const int c = 2 * i;
+    const float2 x = fma2(make_float2(__uint_as_float(rs[c]), __uint_as_float(rs[c + 1])), sc2,
+                          make_float2(nl2(c), nl2(c + 1)));
+    float2 p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+    if (!full) {
+      p.x = visible(c) ? p.x : 0.f;
+      p.y = visible(c + 1) ? p.y : 0.f;
     }
-    pp[i] = FMT == 1 ? pack_bf16x2(p[0], p[1]) : pack_f16x2(p[0], p[1]);
-    pd[i] = FMT == 1 ? pack_bf16x2(ds[0], ds[1]) : pack_f16x2(ds[0], ds[1]);
+    const float2 t = add2(make_float2(__uint_as_float(rd[c]), __uint_as_float(rd[c + 1])),
+                          make_float2(nd(c), nd(c + 1)));
+    const float2 ds = mul2(p, t);
+    pp[i] = FMT == 1 ? pack_bf16x2(p.x, p.y) : pack_f16x2(p.x, p.y);
+    pd[i] = FMT == 1 ? pack_bf16x2(ds.x, ds.y) : pack_f16x2(ds.x, ds.y);
   }
   tmem_st16(s_addr, pp);
   tmem_st16(dp_addr, pd);
@@ -143,7 +149,7 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
   if (threadIdx.x == 0) {
     mbar_init(&bars->fixed, 1);
     for (int s = 0; s < kNS; ++s) {
-      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->full[s], 1 + 32);  // TMA tx arrive + the producer warp's 32 stat writes
       mbar_init(&bars->empty[s], 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -161,27 +167,42 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
+  float2* stats = reinterpret_cast<float2*>(smem + Cfg::kStatOff);
 
   if (warp == 0) {
-    if (lane == 0 && n_it > 0) {
+    if (n_it > 0) {
+      // All 32 lanes: lane 0 issues the TMA copies, every lane stages two of
+      // the 64 (-lse*log2e, -delta) column statistics of the query tile.
       const int kv_plane = b * Hkv + hk;
-      mbar_expect_tx(&bars->fixed, 2 * Cfg::kFixedTile);
-      for (int c = 0; c < Cfg::kBoxes; ++c) {
-        tma_load_3d(smem + Cfg::kFixedOff + c * 128 * 128, &tm_k, &bars->fixed, c * 64, k0, kv_plane);
-        tma_load_3d(smem + Cfg::kFixedOff + Cfg::kFixedTile + c * 128 * 128, &tm_v, &bars->fixed, c * 64, k0,
-                    kv_plane);
+      if (lane == 0) {
+        mbar_expect_tx(&bars->fixed, 2 * Cfg::kFixedTile);
+        for (int c = 0; c < Cfg::kBoxes; ++c) {
+          tma_load_3d(smem + Cfg::kFixedOff + c * 128 * 128, &tm_k, &bars->fixed, c * 64, k0, kv_plane);
+          tma_load_3d(smem + Cfg::kFixedOff + Cfg::kFixedTile + c * 128 * 128, &tm_v, &bars->fixed, c * 64, k0,
+                      kv_plane);
+        }
       }
       for (int it = 0; it < n_it; ++it) {
         const int s = it % kNS;
         if (it >= kNS && !mbar_wait(&bars->empty[s], ((it / kNS) - 1) & 1)) break;
         const int g = it / nqi, qi = i0 + it % nqi;
         const int plane = b * H + hk * G + g;
-        uint8_t* qdst = smem + Cfg::kStreamOff + s * 2 * Cfg::kStreamTile;
-        mbar_expect_tx(&bars->full[s], 2 * Cfg::kStreamTile);
-        for (int c = 0; c < Cfg::kBoxes; ++c) {
-          tma_load_3d(qdst + c * 64 * 128, &tm_q, &bars->full[s], c * 64, qi * 64, plane);
-          tma_load_3d(qdst + Cfg::kStreamTile + c * 64 * 128, &tm_do, &bars->full[s], c * 64, qi * 64, plane);
+        if (lane == 0) {
+          uint8_t* qdst = smem + Cfg::kStreamOff + s * 2 * Cfg::kStreamTile;
+          mbar_expect_tx(&bars->full[s], 2 * Cfg::kStreamTile);
+          for (int c = 0; c < Cfg::kBoxes; ++c) {
+            tma_load_3d(qdst + c * 64 * 128, &tm_q, &bars->full[s], c * 64, qi * 64, plane);
+            tma_load_3d(qdst + Cfg::kStreamTile + c * 64 * 128, &tm_do, &bars->full[s], c * 64, qi * 64, plane);
+          }
         }
+        const long srow = (long)plane * Sq;
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int c = lane + 32 * u, qp = qi * 64 + c;
+          stats[s * 64 + c] = qp < Sq ? make_float2(-lse[srow + qp] * kLog2e, -delta[srow + qp])
+                                      : make_float2(0.f, 0.f);
+        }
+        mbar_arrive(&bars->full[s]);
       }
     }
   } else if (warp == 1) {
@@ -231,28 +252,32 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
     const int row = quad * 32 + lane;  // key row within the tile
     const int kpos = k0 + row;
     const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
-    const float log2e = kLog2e;
     bool ok = true;
     for (int it = 0; it < n_it; ++it) {
-      const int bf = it & 1;
-      const int g = it / nqi, qi = i0 + it % nqi;
+      const int bf = it & 1, st = it % kNS;
+      const int qi = i0 + it % nqi;
       const int q0 = qi * 64 + 32 * w;  // first query column of this thread's half
-      const long srow = (long)(b * H + hk * G + g) * Sq;
-      // Column statistics (identical across the warp: broadcast loads).
-      float l2[32], dl[32];
-#pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        const int qp = q0 + c;
-        l2[c] = qp < Sq ? lse[srow + qp] * log2e : 0.f;
-        dl[c] = qp < Sq ? delta[srow + qp] : 0.f;
-      }
       if (!mbar_wait(&bars->s_full[bf], (it >> 1) & 1)) { ok = false; break; }
       tc_fence_after();
+      // The producer warp wrote this stage's statistics before arriving on its
+      // full barrier; acquire that barrier (already complete, and it cannot
+      // advance before this warpgroup arrives on p_ready) and read them as
+      // broadcast float4 loads.
+      if (!mbar_wait(&bars->full[st], (it / kNS) & 1)) { ok = false; break; }
+      float2 cs[32];
+      const float4* src = reinterpret_cast<const float4*>(stats + st * 64 + 32 * w);
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        const float4 v4 = src[c];
+        cs[2 * c] = make_float2(v4.x, v4.y);
+        cs[2 * c + 1] = make_float2(v4.z, v4.w);
+      }
       const bool key_ok = kpos < kv_len;
+      const bool full = (k0 + 127 < kv_len) && (q0 + 32 <= Sq) && (!causal || q0 >= k0 + 127);
       p_ds_step<FMT>(
-          lane_base + Cfg::kS + bf * 64 + 32 * w, lane_base + Cfg::kDP + bf * 64 + 32 * w, scale_log2,
+          lane_base + Cfg::kS + bf * 64 + 32 * w, lane_base + Cfg::kDP + bf * 64 + 32 * w, scale_log2, full,
           [&](int c) { const int qp = q0 + c; return key_ok && qp < Sq && (!causal || qp >= kpos); },
-          [&](int c) { return l2[c]; }, [&](int c) { return dl[c]; });
+          [&](int c) { return cs[c].x; }, [&](int c) { return cs[c].y; });
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&bars->p_ready[bf]);
@@ -393,8 +418,8 @@ bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     const int qpos = q0 + row;
     const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
     const long srow = (long)bh * Sq + qpos;
-    const float l2 = qpos < Sq ? lse[srow] * kLog2e : 0.f;
-    const float dl = qpos < Sq ? delta[srow] : 0.f;
+    const float nl2 = qpos < Sq ? -lse[srow] * kLog2e : 0.f;
+    const float nd = qpos < Sq ? -delta[srow] : 0.f;
     bool ok = true;
     for (int it = 0; it < n_it; ++it) {
       const int bf = it & 1;
@@ -403,8 +428,9 @@ bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       tc_fence_after();
       int vis = min(32, kv_len - kb);
       if (causal) vis = min(vis, qpos - kb + 1);
+      const bool full = (kb + 32 <= kv_len) && (!causal || kb + 31 <= q0);
       p_ds_step<FMT>(lane_base + Cfg::kS + bf * 64 + 32 * w, lane_base + Cfg::kDP + bf * 64 + 32 * w, scale_log2,
-                     [&](int c) { return c < vis; }, [&](int) { return l2; }, [&](int) { return dl; });
+                     full, [&](int c) { return c < vis; }, [&](int) { return nl2; }, [&](int) { return nd; });
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&bars->p_ready[bf]);

@@ -273,16 +273,22 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         if (causal) vis = min(vis, qpos - k0 + 1);
         vis = max(vis, 0);
       }
-      // Pass 1: row max over the visible scores.
+      // Pass 1: row max over the visible scores (three-input max; the mask
+      // compares are only paid on tiles that touch kv_len or the diagonal).
       float mx = -INFINITY;
 #pragma unroll
       for (int c = 0; c < kBN / 32; ++c) {
         uint32_t r[32];
         tmem_ld32(s_addr + c * 32, r);
         tmem_wait_ld();
+        if (!edge) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (c * 32 + i < vis) mx = fmaxf(mx, __uint_as_float(r[i]));
+          for (int i = 0; i < 32; i += 2) mx = fmax3(mx, __uint_as_float(r[i]), __uint_as_float(r[i + 1]));
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (c * 32 + i < vis) mx = fmaxf(mx, __uint_as_float(r[i]));
+        }
       }
       mx *= scale_log2;
       // Lazy rescale: raise the reference max only when it grew by > 2^8.
@@ -306,9 +312,10 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       }
       // Pass 2: P = 2^(s*scale - m) packed to 16-bit pairs over the first half
       // of the S columns (chunk c's source columns are consumed before any
-      // store reaches them).
+      // store reaches them).  Pairs go through the packed f32x2 FMA/ADD.
       const float msub = (m_run == -INFINITY) ? 0.f : m_run;
-      float rowsum = 0.f;
+      const float2 sc2 = make_float2(scale_log2, scale_log2), nm2 = make_float2(-msub, -msub);
+      float2 rs2 = make_float2(0.f, 0.f);
 #pragma unroll
       for (int c = 0; c < kBN / 64; ++c) {
         uint32_t ra[32], rb[32];
@@ -321,13 +328,18 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
           const uint32_t* src = i < 16 ? ra : rb;
           const int ii = (i % 16) * 2;
           const int col = c * 64 + 2 * i;
-          const float p0 = col < vis ? fast_exp2(fmaf(__uint_as_float(src[ii]), scale_log2, -msub)) : 0.f;
-          const float p1 = col + 1 < vis ? fast_exp2(fmaf(__uint_as_float(src[ii + 1]), scale_log2, -msub)) : 0.f;
-          rowsum += p0 + p1;
-          pk[i] = (fmt == 1) ? pack_bf16x2(p0, p1) : pack_f16x2(p0, p1);
+          const float2 x = fma2(make_float2(__uint_as_float(src[ii]), __uint_as_float(src[ii + 1])), sc2, nm2);
+          float2 p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+          if (edge) {
+            p.x = col < vis ? p.x : 0.f;
+            p.y = col + 1 < vis ? p.y : 0.f;
+          }
+          rs2 = add2(rs2, p);
+          pk[i] = (fmt == 1) ? pack_bf16x2(p.x, p.y) : pack_f16x2(p.x, p.y);
         }
         tmem_st32(s_addr + c * 32, pk);
       }
+      const float rowsum = rs2.x + rs2.y;
       l_run += rowsum;
       tmem_wait_st();
       tc_fence_before();
