@@ -100,3 +100,15 @@ def test_c5_config_generate_cached_and_streaming():
     assert cached.shape == (16, 144) and torch.equal(cached[:, :128], prompts)
     streamed = pf.generate_streaming(params, prompts, 16, cfg, window=512)
     assert torch.equal(streamed, cached)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("head_dim,cache_size", [(128, 32), (64, 512)])
+def test_graph_decode_equals_step_loop(dtype, head_dim, cache_size):
+    """generate_cached replaying one captured CUDA graph == the step-by-step loop."""
+    cfg = _tiny_cfg(n_heads=4, n_kv_heads=2, head_dim=head_dim)
+    params = pf.init_params(9, cfg, dtype=dtype)
+    prompt = torch.tensor([[5, 9, 2, 7, 1], [3, 3, 8, 1, 0]], device="cuda")
+    a = pf.generate_cached(params, prompt, 12, cfg, cache_size=cache_size, use_graph=True)
+    b = pf.generate_cached(params, prompt, 12, cfg, cache_size=cache_size, use_graph=False)
+    assert torch.equal(a, b)

@@ -77,3 +77,13 @@ def test_ring_layout_is_permutation_invariant():
                                        capacity, block_k=capacity)
     assert float((in_order - rolled).abs().max()) < 2e-3
     assert np.max(np.abs(to_np(in_order) - orc.reference_attention(q, k, v))) < 2e-3
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_graph_streaming_equals_step_loop_when_wrapping(dtype):
+    cfg = _cfg(n_heads=4, n_kv_heads=2)
+    params = pf.init_params(3, cfg, dtype=dtype)
+    prompt = torch.tensor([[5, 9, 2, 7, 1, 4, 4, 6, 2, 9, 1]], device="cuda")
+    a = pf.generate_streaming(params, prompt, 30, cfg, window=8, use_graph=True)
+    b = pf.generate_streaming(params, prompt, 30, cfg, window=8, use_graph=False)
+    assert torch.equal(a, b)

@@ -462,7 +462,7 @@ cudaError_t launch_dkv_t(const BwdArgs& a) {
       !make_tile_map(&tdo, a.dout, a.dtype, D, a.Sq, a.Sq, BH, 64))
     return cudaErrorInvalidValue;
   auto kern = bwd_dkv_sm100_kernel<T, D>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
+  cudaError_t e = ensure_smem(kern, Cfg::kSmem);
   if (e != cudaSuccess) return e;
   const int n_kt = (a.Sk + 127) / 128;
   kern<<<n_kt * BHk, kThreads, Cfg::kSmem, a.stream>>>(tk, tv, tq, tdo, a.lse, a.delta, (T*)a.dk, (T*)a.dv, a.H,
@@ -482,7 +482,7 @@ cudaError_t launch_dq_t(const BwdArgs& a) {
       !make_tile_map(&tv, a.v, a.dtype, D, a.kv_len, a.Sk, BHk, 64))
     return cudaErrorInvalidValue;
   auto kern = bwd_dq_sm100_kernel<T, D>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
+  cudaError_t e = ensure_smem(kern, Cfg::kSmem);
   if (e != cudaSuccess) return e;
   const int n_qt = (a.Sq + 127) / 128;
   kern<<<n_qt * BH, kThreads, Cfg::kSmem, a.stream>>>(tq, tdo, tk, tv, a.lse, a.delta, (T*)a.dq, a.H, a.Hkv,

@@ -43,11 +43,14 @@ template <int D>
 struct FwdCfg {
   static constexpr int kBoxes = D / 64;                  // 64-column (128 B) TMA boxes
   static constexpr int kTileBytes = kBM * D * 2;         // one 128 x D 16-bit tile
-  static constexpr int kStages = D == 128 ? 2 : 4;
+  // K and V rings are separate: a K tile is released as soon as both S
+  // MMAs of its step have read it, so K runs further ahead than V.
+  static constexpr int kKStages = D == 128 ? 3 : 4;
+  static constexpr int kVStages = D == 128 ? 2 : 4;
   static constexpr int kQOff = 0;                        // Q0, Q1
   static constexpr int kKOff = 2 * kTileBytes;           // K stages
-  static constexpr int kVOff = kKOff + kStages * kTileBytes;
-  static constexpr int kBarOff = kVOff + kStages * kTileBytes;
+  static constexpr int kVOff = kKOff + kKStages * kTileBytes;
+  static constexpr int kBarOff = kVOff + kVStages * kTileBytes;
   static constexpr int kSmem = kBarOff + 256 + 1024;     // + barriers + alignment slack
   // TMEM columns
   static constexpr uint32_t kS0 = 0, kS1 = 128, kO0 = 256, kO1 = 256 + D;
@@ -57,10 +60,25 @@ struct FwdCfg {
 struct Bars {
   uint64_t q;
   uint64_t q_ready[2];  // RoPE: query tile w rotated in shared memory
-  uint64_t k_full[4], v_full[4], kv_empty[4];
+  uint64_t k_full[4], v_full[4], k_empty[4], v_empty[4];
   uint64_t s_full[2], p_full[2], o_done[2];
   uint32_t tmem_base;
 };
+
+// Eight consecutive table entries [i, i + 8) as floats (16-byte aligned).
+__device__ __forceinline__ void load8_table(const void* t, int dtype, long i, float (&o)[8]) {
+  if (dtype == PF_F32) {
+    const float4 a = *reinterpret_cast<const float4*>(static_cast<const float*>(t) + i);
+    const float4 b = *reinterpret_cast<const float4*>(static_cast<const float*>(t) + i + 4);
+    o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w; o[4] = b.x; o[5] = b.y; o[6] = b.z; o[7] = b.w;
+  } else {
+    uint4 raw = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(t) + i);
+    const uint16_t* h = reinterpret_cast<const uint16_t*>(&raw);
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      o[u] = dtype == PF_BF16 ? __bfloat162float(__ushort_as_bfloat16(h[u])) : __half2float(__ushort_as_half(h[u]));
+  }
+}
 
 // Rotates one query row of a swizzled 128 x D tile in place:
 // x*cos + rotate_half(x)*sin with table row `pos` (fused_rope.py:43-50, :75-78).
@@ -76,14 +94,16 @@ __device__ __forceinline__ void rope_row_in_smem(uint8_t* tile, int row, const v
     uint4 v0 = *p0, v1 = *p1;
     T* x0 = reinterpret_cast<T*>(&v0);
     T* x1 = reinterpret_cast<T*>(&v1);
+    float c0[8], s0[8], c1[8], s1[8];
+    load8_table(cos_t, tbl_dtype, pos * D + d0, c0);
+    load8_table(sin_t, tbl_dtype, pos * D + d0, s0);
+    load8_table(cos_t, tbl_dtype, pos * D + d1, c1);
+    load8_table(sin_t, tbl_dtype, pos * D + d1, s1);
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
       const float a = to_f(x0[u]), bb = to_f(x1[u]);
-      const long i0 = pos * D + d0 + u, i1 = pos * D + d1 + u;
-      const float r0 = a * load_any(cos_t, tbl_dtype, i0) - bb * load_any(sin_t, tbl_dtype, i0);
-      const float r1 = bb * load_any(cos_t, tbl_dtype, i1) + a * load_any(sin_t, tbl_dtype, i1);
-      x0[u] = from_f<T>(r0);
-      x1[u] = from_f<T>(r1);
+      x0[u] = from_f<T>(a * c0[u] - bb * s0[u]);
+      x1[u] = from_f<T>(bb * c1[u] + a * s1[u]);
     }
     *p0 = v0;
     *p1 = v1;
@@ -97,7 +117,7 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
                  float* __restrict__ lse, int B, int H, int Hkv, int Sq, int kv_len, int causal,
                  float scale_log2, int n_qtiles, const void* q_cos, const void* q_sin, int tbl_dtype) {
   using Cfg = FwdCfg<D>;
-  constexpr int NS = Cfg::kStages;
+  constexpr int KS = Cfg::kKStages, VS = Cfg::kVStages;
   constexpr int fmt = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
   constexpr uint32_t idesc_qk = make_idesc_f16(fmt, kBM, kBN, 0, 0);
   constexpr uint32_t idesc_pv = make_idesc_f16(fmt, kBM, D, 0, 1);
@@ -134,10 +154,11 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     mbar_init(&bars->q, 1);
     mbar_init(&bars->q_ready[0], kBM);
     mbar_init(&bars->q_ready[1], kBM);
-    for (int s = 0; s < NS; ++s) {
+    for (int s = 0; s < 4; ++s) {
       mbar_init(&bars->k_full[s], 1);
       mbar_init(&bars->v_full[s], 1);
-      mbar_init(&bars->kv_empty[s], 1);
+      mbar_init(&bars->k_empty[s], 1);
+      mbar_init(&bars->v_empty[s], 1);
     }
     for (int w = 0; w < 2; ++w) {
       mbar_init(&bars->s_full[w], 1);
@@ -170,17 +191,29 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
                       c * 64, q_start + w * kBM, bh);
       }
       const int kv_plane = b * Hkv + hk;
-      for (int j = 0; j < n_max; ++j) {
-        const int s = j % NS;
-        if (j >= NS && !mbar_wait(&bars->kv_empty[s], ((j / NS) - 1) & 1)) break;
+      // Issue order K0, K1, V0, K2, V1, ...: K one step ahead of V.
+      auto load_k = [&](int j) -> bool {
+        const int s = j % KS;
+        if (j >= KS && !mbar_wait(&bars->k_empty[s], ((j / KS) - 1) & 1)) return false;
         mbar_expect_tx(&bars->k_full[s], Cfg::kTileBytes);
         for (int c = 0; c < Cfg::kBoxes; ++c)
           tma_load_3d(smem + Cfg::kKOff + s * Cfg::kTileBytes + c * kBN * 128, &tm_k,
                       &bars->k_full[s], c * 64, j * kBN, kv_plane);
+        return true;
+      };
+      auto load_v = [&](int j) -> bool {
+        const int s = j % VS;
+        if (j >= VS && !mbar_wait(&bars->v_empty[s], ((j / VS) - 1) & 1)) return false;
         mbar_expect_tx(&bars->v_full[s], Cfg::kTileBytes);
         for (int c = 0; c < Cfg::kBoxes; ++c)
           tma_load_3d(smem + Cfg::kVOff + s * Cfg::kTileBytes + c * kBN * 128, &tm_v,
                       &bars->v_full[s], c * 64, j * kBN, kv_plane);
+        return true;
+      };
+      bool okp = n_max > 0 ? load_k(0) : true;
+      for (int j = 1; okp && j <= n_max; ++j) {
+        if (j < n_max) okp = load_k(j);
+        okp = okp && load_v(j - 1);
       }
     }
   } else if (warp == 1) {
@@ -198,7 +231,7 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       const uint32_t s_col[2] = {Cfg::kS0, Cfg::kS1};
       const uint32_t o_col[2] = {Cfg::kO0, Cfg::kO1};
       auto issue_s = [&](int w, int j) {
-        const uint32_t k_addr = sbase + Cfg::kKOff + (j % NS) * Cfg::kTileBytes;
+        const uint32_t k_addr = sbase + Cfg::kKOff + (j % KS) * Cfg::kTileBytes;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk)
           umma_ss(tmem + s_col[w], desc_k<kBM>(q_addr[w], kk), desc_k<kBN>(k_addr, kk),
@@ -206,7 +239,7 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         umma_commit(&bars->s_full[w]);
       };
       auto issue_pv = [&](int w, int j) {
-        const uint32_t v_addr = sbase + Cfg::kVOff + (j % NS) * Cfg::kTileBytes;
+        const uint32_t v_addr = sbase + Cfg::kVOff + (j % VS) * Cfg::kTileBytes;
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk)
           umma_ts(tmem + o_col[w], tmem + s_col[w] + kk * 8, desc_mn<kBN>(v_addr, kk), idesc_pv,
@@ -214,29 +247,35 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         umma_commit(&bars->o_done[w]);
       };
       for (int j = 0; ok && j <= n_max; ++j) {
-        const int s = j % NS;
+        const int ks = j % KS, vs = j % VS;
         const bool need_k = (j < n_w[0]) || (j < n_w[1]);
         if (need_k) {
-          ok = mbar_wait(&bars->k_full[s], (j / NS) & 1);
+          ok = mbar_wait(&bars->k_full[ks], (j / KS) & 1);
           if (!ok) break;
           tc_fence_after();
         }
-        if (j < n_w[0]) issue_s(0, j);
+        if (j < n_w[0]) {
+          issue_s(0, j);
+          if (j >= n_w[1]) umma_commit(&bars->k_empty[ks]);  // only reader of K_j
+        }
         if (j >= 1 && j - 1 < n_w[1]) {
-          const int sp = (j - 1) % NS;
-          ok = mbar_wait(&bars->p_full[1], (j - 1) & 1) && mbar_wait(&bars->v_full[sp], ((j - 1) / NS) & 1);
+          const int vp = (j - 1) % VS;
+          ok = mbar_wait(&bars->p_full[1], (j - 1) & 1) && mbar_wait(&bars->v_full[vp], ((j - 1) / VS) & 1);
           if (!ok) break;
           tc_fence_after();
           issue_pv(1, j - 1);
-          umma_commit(&bars->kv_empty[sp]);  // last reader of stage j-1
+          umma_commit(&bars->v_empty[vp]);  // last reader of V_{j-1}
         }
-        if (j < n_w[1]) issue_s(1, j);
+        if (j < n_w[1]) {
+          issue_s(1, j);
+          umma_commit(&bars->k_empty[ks]);  // last reader of K_j
+        }
         if (j < n_w[0]) {
-          ok = mbar_wait(&bars->p_full[0], j & 1) && mbar_wait(&bars->v_full[s], (j / NS) & 1);
+          ok = mbar_wait(&bars->p_full[0], j & 1) && mbar_wait(&bars->v_full[vs], (j / VS) & 1);
           if (!ok) break;
           tc_fence_after();
           issue_pv(0, j);
-          if (j >= n_w[1]) umma_commit(&bars->kv_empty[s]);
+          if (j >= n_w[1]) umma_commit(&bars->v_empty[vs]);
         }
       }
     }
@@ -391,7 +430,7 @@ cudaError_t launch_t(const FwdArgs& a, const void* k_rot) {
       !make_tile_map(&tv, a.v, a.dtype, D, a.kv_len, a.Sk, a.B * a.Hkv, kBN))
     return cudaErrorInvalidValue;
   auto kern = fwd_sm100_kernel<T, D, ROPE>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
+  cudaError_t e = ensure_smem(kern, Cfg::kSmem);
   if (e != cudaSuccess) return e;
   const int n_qtiles = (a.Sq + 2 * kBM - 1) / (2 * kBM);
   dim3 grid((unsigned)(n_qtiles * a.B * a.H));
@@ -420,14 +459,16 @@ __global__ void rope_rows_kernel(const T* __restrict__ x, T* __restrict__ out, c
     uint4 v1 = *reinterpret_cast<const uint4*>(x + base + d1);
     T* x0 = reinterpret_cast<T*>(&v0);
     T* x1 = reinterpret_cast<T*>(&v1);
+    float c0[8], s0[8], c1[8], s1[8];
+    load8_table(cos_t, tbl_dtype, (long)pos * D + d0, c0);
+    load8_table(sin_t, tbl_dtype, (long)pos * D + d0, s0);
+    load8_table(cos_t, tbl_dtype, (long)pos * D + d1, c1);
+    load8_table(sin_t, tbl_dtype, (long)pos * D + d1, s1);
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
       const float a = to_f(x0[u]), bb = to_f(x1[u]);
-      const long i0 = (long)pos * D + d0 + u, i1 = (long)pos * D + d1 + u;
-      const float r0 = a * load_any(cos_t, tbl_dtype, i0) - bb * load_any(sin_t, tbl_dtype, i0);
-      const float r1 = bb * load_any(cos_t, tbl_dtype, i1) + a * load_any(sin_t, tbl_dtype, i1);
-      x0[u] = from_f<T>(r0);
-      x1[u] = from_f<T>(r1);
+      x0[u] = from_f<T>(a * c0[u] - bb * s0[u]);
+      x1[u] = from_f<T>(bb * c1[u] + a * s1[u]);
     }
     *reinterpret_cast<uint4*>(out + base + d0) = v0;
     *reinterpret_cast<uint4*>(out + base + d1) = v1;

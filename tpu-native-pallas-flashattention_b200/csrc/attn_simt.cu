@@ -328,7 +328,7 @@ cudaError_t launch_fwd_t(const FwdArgs& a) {
   constexpr int LD = DMAX + 1;
   const size_t smem = (size_t)(kBQ + 2 * kBK) * LD * sizeof(float);
   auto kern = fwd_simt_kernel<T, DMAX>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t e = ensure_smem(kern, (int)smem);
   if (e != cudaSuccess) return e;
   dim3 grid((a.Sq + kBQ - 1) / kBQ, a.H, a.B);
   kern<<<grid, kThreads, smem, a.stream>>>(
@@ -342,7 +342,7 @@ cudaError_t launch_dq_t(const BwdArgs& a) {
   constexpr int LD = DMAX + 1;
   const size_t smem = (size_t)(2 * kBQ + 2 * kBK) * LD * sizeof(float);
   auto kern = bwd_dq_simt_kernel<T, DMAX>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t e = ensure_smem(kern, (int)smem);
   if (e != cudaSuccess) return e;
   dim3 grid((a.Sq + kBQ - 1) / kBQ, a.H, a.B);
   kern<<<grid, kThreads, smem, a.stream>>>((const T*)a.q, (const T*)a.k, (const T*)a.v,
@@ -356,7 +356,7 @@ cudaError_t launch_dkv_t(const BwdArgs& a) {
   constexpr int LD = DMAX + 1;
   const size_t smem = ((size_t)(2 * kBK + 2 * kBQ) * LD + 2 * kBQ * (kBK + 1) + 2 * kBQ) * sizeof(float);
   auto kern = bwd_dkv_simt_kernel<T, DMAX>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t e = ensure_smem(kern, (int)smem);
   if (e != cudaSuccess) return e;
   dim3 grid((a.Sk + kBK - 1) / kBK, a.Hkv, a.B);
   kern<<<grid, kThreads, smem, a.stream>>>((const T*)a.q, (const T*)a.k, (const T*)a.v,

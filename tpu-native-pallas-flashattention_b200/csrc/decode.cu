@@ -274,7 +274,7 @@ cudaError_t launch_decode_t(const DecodeArgs& a) {
   const size_t smem = Cfg::kSmemRing + (size_t)GC * D * 4 + (size_t)Cfg::kWarps * GC * (D + 2) * 4 +
                       (size_t)Cfg::kWarps * Cfg::kStages * 8;
   auto kern = decode_split_kernel<T, D, GC>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t e = ensure_smem(kern, (int)smem);
   if (e != cudaSuccess) return e;
   dim3 grid(a.num_splits, a.Hkv * head_chunks, a.B);
   kern<<<grid, Cfg::kWarps * 32, smem, a.stream>>>(a, head_chunks);

@@ -344,7 +344,7 @@ cudaError_t launch_tc_t(const DecodeArgs& a) {
   const int G = a.H / a.Hkv;
   const int head_chunks = (G + 15) / 16;
   auto kern = decode_tc_kernel<T, D>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
+  cudaError_t e = ensure_smem(kern, Cfg::kSmem);
   if (e != cudaSuccess) return e;
   dim3 grid(a.num_splits, a.Hkv * head_chunks, a.B);
   kern<<<grid, kWarps * 32, Cfg::kSmem, a.stream>>>(a, tk, tv, head_chunks, seg_rows);

@@ -89,6 +89,14 @@ cudaError_t launch_paged_gather(const void* pages, const int32_t* block_tables, 
                                 int dtype, int B, int Hkv, int num_pages, int page_size,
                                 int pages_per_seq, int D, cudaStream_t stream);
 
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (kernel, device):
+// later launches -- including ones recorded into a CUDA graph -- skip the call.
+cudaError_t set_smem_once(const void* kernel, int bytes);
+template <typename K>
+inline cudaError_t ensure_smem(K kernel, int bytes) {
+  return set_smem_once(reinterpret_cast<const void*>(kernel), bytes);
+}
+
 // Records the message returned by pf_last_error() and returns `code`.
 int set_last_error(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
 

@@ -1,6 +1,11 @@
 // sm100_util.cu -- host side of sm100_util.cuh: TMA tensor maps, encoded
 // through the driver entry point so the library needs no -lcuda.
 #include "sm100_util.cuh"
+#include "kernels.h"
+
+#include <mutex>
+#include <set>
+#include <utility>
 
 namespace pf {
 namespace {
@@ -25,6 +30,19 @@ EncodeTiledFn get_encode_fn() {
 }
 
 }  // namespace
+
+cudaError_t set_smem_once(const void* kernel, int bytes) {
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.count({kernel, dev})) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done.insert({kernel, dev});
+  return e;
+}
 
 bool make_tile_map(CUtensorMap* m, const void* base, int dtype, int D, int rows,
                    long row_stride_rows, int planes, int box_rows) {

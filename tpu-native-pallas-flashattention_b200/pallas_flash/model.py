@@ -28,6 +28,7 @@ import torch
 from . import _lib
 from .config import ModelConfig
 from .flash_attention import flash_attention, flash_attention_decode
+from .paged import paged_flash_attention, write_to_paged_cache_batch
 
 Params = Dict[str, Any]
 Cache = list  # per-layer list of {"k": [b, n_kv, cache_size, d], "v": same}
@@ -264,17 +265,109 @@ def decode_step(params: Params, token, cache: Cache, pos: int, cfg: ModelConfig,
     return _decode_layers(params, token, cache, pos, pos, pos + 1, cfg)
 
 
+class DecodeGraph:
+    """One decode step of every layer, captured once as a CUDA graph and replayed per token.
+
+    A Python decode step issues ~100 small launches (8 layers of norms,
+    projections, RoPE, cache write, attention, MLP); at batch 16 the host loop,
+    not the GPU, sets the token rate.  Here the position lives on the device:
+    the fixed (or ring) cache ``[B, Hkv, C, D]`` is addressed as a page pool of
+    one ``C``-token page per sequence, the cache write goes through the paged
+    write kernel at slot ``pos % C`` and attention through the paged decode
+    kernel with device lengths ``min(pos + 1, C)``, so one captured graph
+    serves every position.  Kernels, split schedule and RoPE tables are those
+    of ``decode_step`` / ``ring_decode_step``.
+    """
+
+    def __init__(self, params: Params, cache: Cache, cfg: ModelConfig, batch: int, dtype, device):
+        self.params, self.cache, self.cfg = params, cache, cfg
+        self.C = cache[0]["k"].shape[2]
+        self.token = torch.zeros((batch, 1), dtype=torch.long, device=device)
+        self.pos = torch.zeros((1,), dtype=torch.long, device=device)
+        self.table = torch.arange(batch, dtype=torch.int32, device=device).reshape(batch, 1)
+        self.slots = torch.zeros((batch,), dtype=torch.int32, device=device)
+        self.lens = torch.zeros((batch,), dtype=torch.int32, device=device)
+        self.dtype, self.device = dtype, device
+        self.graph = None
+
+    def _tables(self, last_pos: int):
+        # rows are gathered from the table _rope_slice caches (same values, same dtype)
+        self.cos, self.sin = _rope_slice(0, last_pos + 1, self.cfg, self.dtype, self.device)
+
+    def _step(self):
+        cfg, p = self.cfg, self.params
+        self.slots.copy_((self.pos % self.C).to(torch.int32).expand_as(self.slots))
+        self.lens.copy_(torch.clamp(self.pos + 1, max=self.C).to(torch.int32).expand_as(self.lens))
+        x = p["embed"][self.token]
+        cos = self.cos.index_select(0, self.pos)
+        sin = self.sin.index_select(0, self.pos)
+        batch = x.shape[0]
+        for layer, lc in zip(p["layers"], self.cache):
+            h = rms_norm(x, layer["attn_norm"], cfg.rms_norm_eps)
+            q, k, v = project_qkv(layer, h, cfg)
+            q = apply_rope(q, cos, sin)
+            k = apply_rope(k, cos, sin)
+            write_to_paged_cache_batch(lc["k"], lc["v"], k, v, self.table, self.slots)
+            attn = paged_flash_attention(q, lc["k"], lc["v"], self.table, self.lens, max_context_len=self.C)
+            x = x + attn.transpose(1, 2).reshape(batch, 1, cfg.dim) @ layer["wo"]
+            h = rms_norm(x, layer["ffn_norm"], cfg.rms_norm_eps)
+            x = x + swiglu_mlp(h, layer["w_gate"], layer["w_up"], layer["w_down"])
+        x = rms_norm(x, p["final_norm"], cfg.rms_norm_eps)
+        self.token.copy_(_argmax_last(x @ p["lm_head"]))
+        self.pos.add_(1)
+
+    def capture(self, token, pos: int, last_pos: int):
+        """One eager warm-up step at ``pos`` (it writes cache slot ``pos`` with the values the
+        first replay writes there), then the capture of that step."""
+        self._tables(last_pos)
+        side = torch.cuda.Stream(device=self.device)
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            self.token.copy_(token)
+            self.pos.fill_(pos)
+            self._step()
+        torch.cuda.current_stream().wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self._step()
+        self.token.copy_(token)
+        self.pos.fill_(pos)
+
+    def replay(self):
+        self.graph.replay()
+        return self.token
+
+
+def _generate_graph(params: Params, prompt_ids, max_new_tokens: int, cfg: ModelConfig, logits, cache):
+    batch, prompt_len = prompt_ids.shape
+    next_tok = _argmax_last(logits).to(prompt_ids.dtype)
+    out = torch.empty((batch, prompt_len + max_new_tokens), dtype=prompt_ids.dtype, device=prompt_ids.device)
+    out[:, :prompt_len] = prompt_ids
+    out[:, prompt_len:prompt_len + 1] = next_tok
+    if max_new_tokens > 1:
+        g = DecodeGraph(params, cache, cfg, batch, params["embed"].dtype, prompt_ids.device)
+        g.capture(next_tok, prompt_len, prompt_len + max_new_tokens)
+        for i in range(max_new_tokens - 1):
+            out[:, prompt_len + 1 + i:prompt_len + 2 + i] = g.replay()
+    return out
+
+
 def generate_cached(params: Params, prompt_ids, max_new_tokens: int, cfg: ModelConfig,
-                    interpret: bool = False, cache_size: Optional[int] = None):
+                    interpret: bool = False, cache_size: Optional[int] = None, use_graph: bool = True):
     """Greedy generation with a fixed-size KV cache (model.py:359-386).
 
     ``cache_size`` defaults to ``prompt_len + max_new_tokens`` as in the
-    reference; a larger capacity (e.g. 512) may be given.
+    reference; a larger capacity (e.g. 512) may be given.  With ``use_graph``
+    (default) the decode steps replay one captured CUDA graph (``DecodeGraph``).
     """
     batch, prompt_len = prompt_ids.shape
     if cache_size is None:
         cache_size = prompt_len + max_new_tokens
     logits, cache = prefill(params, prompt_ids, cfg, cache_size=cache_size)
+    if use_graph:
+        if prompt_len + max_new_tokens - 1 > cache_size:
+            raise ValueError(f"position {prompt_len + max_new_tokens - 2} exceeds cache capacity {cache_size}")
+        return _generate_graph(params, prompt_ids, max_new_tokens, cfg, logits, cache)
     next_tok = _argmax_last(logits).to(prompt_ids.dtype)
     out = [prompt_ids, next_tok]
     for i in range(max_new_tokens - 1):
@@ -329,10 +422,17 @@ def ring_decode_step(params: Params, token, cache: Cache, pos: int, cfg: ModelCo
 
 
 def generate_streaming(params: Params, prompt_ids, max_new_tokens: int, cfg: ModelConfig,
-                       window: int, interpret: bool = False):
-    """Greedy generation in constant memory with a ring-buffer cache of ``window`` slots."""
+                       window: int, interpret: bool = False, use_graph: bool = True):
+    """Greedy generation in constant memory with a ring-buffer cache of ``window`` slots.
+
+    With ``use_graph`` (default) the decode steps replay one captured CUDA graph
+    whose slot ``pos % window`` and live length ``min(pos + 1, window)`` are
+    computed on the device.
+    """
     batch, prompt_len = prompt_ids.shape
     logits, cache = prefill_ring(params, prompt_ids, cfg, window)
+    if use_graph:
+        return _generate_graph(params, prompt_ids, max_new_tokens, cfg, logits, cache)
     next_tok = _argmax_last(logits).to(prompt_ids.dtype)
     out: List[torch.Tensor] = [prompt_ids, next_tok]
     for i in range(max_new_tokens - 1):
