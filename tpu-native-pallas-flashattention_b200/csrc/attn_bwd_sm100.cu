@@ -215,6 +215,7 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
           const int s = it % kNS, bf = it & 1;
           ok = mbar_wait(&bars->full[s], (it / kNS) & 1);
           if (!ok) break;
+          trace(1, it);
           tc_fence_after();
           const uint32_t q_addr = sbase + Cfg::kStreamOff + s * 2 * Cfg::kStreamTile;
           const uint32_t do_addr = q_addr + Cfg::kStreamTile;
@@ -225,11 +226,13 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
           for (int kk = 0; kk < D / 16; ++kk)
             umma_ss(tmem + Cfg::kDP + bf * 64, desc_k<128>(v_addr, kk), desc_k<64>(do_addr, kk), idesc_s, kk > 0);
           umma_commit(&bars->s_full[bf]);
+          trace(2, it);
         }
         if (it >= 1) {
           const int j = it - 1, s = j % kNS, bf = j & 1;
           ok = mbar_wait(&bars->p_ready[bf], (j >> 1) & 1);
           if (!ok) break;
+          trace(3, j);
           tc_fence_after();
           const uint32_t q_addr = sbase + Cfg::kStreamOff + s * 2 * Cfg::kStreamTile;
           const uint32_t do_addr = q_addr + Cfg::kStreamTile;
@@ -242,6 +245,7 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
             umma_ts(tmem + Cfg::kAcc + D, tmem + Cfg::kDP + bf * 64 + split_packed_col(kk), desc_mn<64>(q_addr, kk),
                     idesc_acc, (j > 0 || kk > 0));
           umma_commit(&bars->empty[s]);
+          trace(4, j);
         }
       }
       umma_commit(&bars->done);
@@ -258,6 +262,7 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
       const int qi = i0 + it % nqi;
       const int q0 = qi * 64 + 32 * w;  // first query column of this thread's half
       if (!mbar_wait(&bars->s_full[bf], (it >> 1) & 1)) { ok = false; break; }
+      if (threadIdx.x == 128 || threadIdx.x == 256) trace(8 + 2 * w, it);
       tc_fence_after();
       // The producer warp wrote this stage's statistics before arriving on its
       // full barrier; acquire that barrier (already complete, and it cannot
@@ -280,6 +285,7 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
           [&](int c) { return cs[c].x; }, [&](int c) { return cs[c].y; });
       tmem_wait_st();
       tc_fence_before();
+      if (threadIdx.x == 128 || threadIdx.x == 256) trace(9 + 2 * w, it);
       mbar_arrive(&bars->p_ready[bf]);
     }
     // Epilogue: warpgroup 0 writes dV, warpgroup 1 writes dK (scaled).

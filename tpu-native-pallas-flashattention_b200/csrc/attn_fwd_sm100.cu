@@ -36,7 +36,7 @@ namespace {
 
 constexpr int kBM = 128;        // rows per query tile (= TMEM lanes)
 constexpr int kBN = 128;        // keys per kv tile
-constexpr int kThreads = 384;   // 12 warps
+constexpr int kThreads = 320;   // 10 warps: 0-7 softmax, 8 TMA, 9 MMA
 constexpr float kRescaleThresh = 8.0f;  // log2 units
 
 template <int D>
@@ -167,7 +167,7 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     }
     fence_barrier_init();
   }
-  if (warp == 1) {
+  if (warp == 9) {
     tmem_alloc(&bars->tmem_base, Cfg::kTmemCols);
     tmem_relinquish();
   }
@@ -176,7 +176,7 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
 
-  if (warp == 0) {
+  if (warp == 8) {
     // ------------------------------ producer ------------------------------
     if (lane == 0) {
       tma_prefetch_desc(&tm_q);
@@ -199,6 +199,7 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         for (int c = 0; c < Cfg::kBoxes; ++c)
           tma_load_3d(smem + Cfg::kKOff + s * Cfg::kTileBytes + c * kBN * 128, &tm_k,
                       &bars->k_full[s], c * 64, j * kBN, kv_plane);
+        trace(12, j);
         return true;
       };
       auto load_v = [&](int j) -> bool {
@@ -208,6 +209,7 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         for (int c = 0; c < Cfg::kBoxes; ++c)
           tma_load_3d(smem + Cfg::kVOff + s * Cfg::kTileBytes + c * kBN * 128, &tm_v,
                       &bars->v_full[s], c * 64, j * kBN, kv_plane);
+        trace(13, j);
         return true;
       };
       bool okp = n_max > 0 ? load_k(0) : true;
@@ -216,7 +218,7 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         okp = okp && load_v(j - 1);
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == 9) {
     // ------------------------------ MMA issuer ----------------------------
     if (lane == 0 && n_max > 0) {
       bool ok = true;
@@ -250,38 +252,43 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         const int ks = j % KS, vs = j % VS;
         const bool need_k = (j < n_w[0]) || (j < n_w[1]);
         if (need_k) {
-          ok = mbar_wait(&bars->k_full[ks], (j / KS) & 1);
+          ok = mbar_wait_spin(&bars->k_full[ks], (j / KS) & 1);
           if (!ok) break;
+          trace(1, j);
           tc_fence_after();
         }
         if (j < n_w[0]) {
           issue_s(0, j);
+          trace(2, j);
           if (j >= n_w[1]) umma_commit(&bars->k_empty[ks]);  // only reader of K_j
         }
         if (j >= 1 && j - 1 < n_w[1]) {
           const int vp = (j - 1) % VS;
-          ok = mbar_wait(&bars->p_full[1], (j - 1) & 1) && mbar_wait(&bars->v_full[vp], ((j - 1) / VS) & 1);
+          ok = mbar_wait_spin(&bars->p_full[1], (j - 1) & 1) && mbar_wait_spin(&bars->v_full[vp], ((j - 1) / VS) & 1);
           if (!ok) break;
+          trace(3, j - 1);
           tc_fence_after();
           issue_pv(1, j - 1);
           umma_commit(&bars->v_empty[vp]);  // last reader of V_{j-1}
         }
         if (j < n_w[1]) {
           issue_s(1, j);
+          trace(5, j);
           umma_commit(&bars->k_empty[ks]);  // last reader of K_j
         }
         if (j < n_w[0]) {
-          ok = mbar_wait(&bars->p_full[0], j & 1) && mbar_wait(&bars->v_full[vs], (j / VS) & 1);
+          ok = mbar_wait_spin(&bars->p_full[0], j & 1) && mbar_wait_spin(&bars->v_full[vs], (j / VS) & 1);
           if (!ok) break;
+          trace(6, j);
           tc_fence_after();
           issue_pv(0, j);
           if (j >= n_w[1]) umma_commit(&bars->v_empty[vs]);
         }
       }
     }
-  } else if (warp >= 4) {
+  } else if (warp < 8) {
     // ------------------------------ softmax -------------------------------
-    const int w = (warp - 4) / 4;           // query tile of this warpgroup
+    const int w = warp / 4;                 // query tile of this warpgroup
     const int quad = warp % 4;              // TMEM lane quadrant
     const int row = quad * 32 + lane;       // row within the tile
     const int qpos = q_start + w * kBM + row;
@@ -300,7 +307,8 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       mbar_arrive(&bars->q_ready[w]);
     }
     for (int j = 0; ok && j < n; ++j) {
-      if (!mbar_wait(&bars->s_full[w], j & 1)) { ok = false; break; }
+      if (!mbar_wait_spin(&bars->s_full[w], j & 1)) { ok = false; break; }
+      if (threadIdx.x == 0 || threadIdx.x == 128) trace(8 + 2 * w, j);
       tc_fence_after();
       const int k0 = j * kBN;
       const bool edge = (k0 + kBN > kv_len) || (causal && k0 + kBN - 1 > q_start + w * kBM);
@@ -312,24 +320,29 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         if (causal) vis = min(vis, qpos - k0 + 1);
         vis = max(vis, 0);
       }
-      // Pass 1: row max over the visible scores (three-input max; the mask
-      // compares are only paid on tiles that touch kv_len or the diagonal).
-      float mx = -INFINITY;
+      // Pass 1: row max.  All four 32-column loads are in flight before the
+      // single wait; four independent three-input max chains.
+      float mx;
+      {
+        uint32_t r[kBN / 32][32];
 #pragma unroll
-      for (int c = 0; c < kBN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(s_addr + c * 32, r);
+        for (int c = 0; c < kBN / 32; ++c) tmem_ld32(s_addr + c * 32, r[c]);
         tmem_wait_ld();
-        if (!edge) {
+        if (edge) {
 #pragma unroll
-          for (int i = 0; i < 32; i += 2) mx = fmax3(mx, __uint_as_float(r[i]), __uint_as_float(r[i + 1]));
-        } else {
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (c * 32 + i < vis) mx = fmaxf(mx, __uint_as_float(r[i]));
+          for (int i = 0; i < kBN; ++i)
+            if (i >= vis) r[i >> 5][i & 31] = __float_as_uint(-INFINITY);
         }
+        float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+        for (int i = 0; i < kBN; i += 8) {
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            mq[u] = fmax3(mq[u], __uint_as_float(r[(i + 2 * u) >> 5][(i + 2 * u) & 31]),
+                          __uint_as_float(r[(i + 2 * u + 1) >> 5][(i + 2 * u + 1) & 31]));
+        }
+        mx = fmax3(mq[0], mq[1], fmaxf(mq[2], mq[3])) * scale_log2;
       }
-      mx *= scale_log2;
       // Lazy rescale: raise the reference max only when it grew by > 2^8.
       const bool upd = mx > m_run + kRescaleThresh;
       const float alpha = upd ? fast_exp2(m_run - mx) : 1.f;  // 0 when m_run = -inf
@@ -341,47 +354,50 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         // PV of tile j-1 is complete: its commit preceded S_w(j)'s.
 #pragma unroll
         for (int c = 0; c < D / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld32(o_addr + c * 32, r);
+          uint32_t o[32];
+          tmem_ld32(o_addr + c * 32, o);
           tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-          tmem_st32(o_addr + c * 32, r);
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st32(o_addr + c * 32, o);
         }
       }
-      // Pass 2: P = 2^(s*scale - m) packed to 16-bit pairs over the first half
-      // of the S columns (chunk c's source columns are consumed before any
-      // store reaches them).  Pairs go through the packed f32x2 FMA/ADD.
+      // Pass 2: P = 2^(s*scale - m) in 64-column halves (two loads, one wait
+      // each), packed to 16-bit pairs into the first half of the S columns
+      // (a half's source columns are consumed before any store reaches them);
+      // the row sum runs in four independent packed accumulators.
       const float msub = (m_run == -INFINITY) ? 0.f : m_run;
       const float2 sc2 = make_float2(scale_log2, scale_log2), nm2 = make_float2(-msub, -msub);
-      float2 rs2 = make_float2(0.f, 0.f);
+      float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                       make_float2(0.f, 0.f)};
 #pragma unroll
       for (int c = 0; c < kBN / 64; ++c) {
-        uint32_t ra[32], rb[32];
-        tmem_ld32(s_addr + c * 64, ra);
-        tmem_ld32(s_addr + c * 64 + 32, rb);
+        uint32_t ra[2][32];
+        tmem_ld32(s_addr + c * 64, ra[0]);
+        tmem_ld32(s_addr + c * 64 + 32, ra[1]);
         tmem_wait_ld();
         uint32_t pk[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const uint32_t* src = i < 16 ? ra : rb;
-          const int ii = (i % 16) * 2;
-          const int col = c * 64 + 2 * i;
-          const float2 x = fma2(make_float2(__uint_as_float(src[ii]), __uint_as_float(src[ii + 1])), sc2, nm2);
+          const int cl = 2 * i, col = c * 64 + cl;
+          const float2 x = fma2(make_float2(__uint_as_float(ra[cl >> 5][cl & 31]),
+                                            __uint_as_float(ra[(cl + 1) >> 5][(cl + 1) & 31])), sc2, nm2);
           float2 p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
           if (edge) {
             p.x = col < vis ? p.x : 0.f;
             p.y = col + 1 < vis ? p.y : 0.f;
           }
-          rs2 = add2(rs2, p);
+          acc[i & 3] = add2(acc[i & 3], p);
           pk[i] = (fmt == 1) ? pack_bf16x2(p.x, p.y) : pack_f16x2(p.x, p.y);
         }
         tmem_st32(s_addr + c * 32, pk);
       }
+      const float2 rs2 = add2(add2(acc[0], acc[1]), add2(acc[2], acc[3]));
       const float rowsum = rs2.x + rs2.y;
       l_run += rowsum;
       tmem_wait_st();
       tc_fence_before();
+      if (threadIdx.x == 0 || threadIdx.x == 128) trace(9 + 2 * w, j);
       mbar_arrive(&bars->p_full[w]);
     }
     // ------------------------------ epilogue ------------------------------
@@ -414,7 +430,7 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == 9) {
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, Cfg::kTmemCols);

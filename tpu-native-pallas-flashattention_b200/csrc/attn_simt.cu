@@ -18,6 +18,10 @@
 namespace pf {
 
 __device__ int g_status = 0;
+#ifdef PF_TRACE
+__device__ unsigned long long g_trace[kTraceCtas * kTraceEvents];
+__device__ unsigned int g_trace_n[kTraceCtas];
+#endif
 
 namespace {
 

@@ -83,6 +83,17 @@ int pf_device_status(int* bits_out, int reset) {
   return PF_OK;
 }
 
+#ifdef PF_TRACE
+// Development builds only: copies the phase trace out and clears it.
+int pf_trace_read(unsigned long long* dst, unsigned int* counts) {
+  cudaDeviceSynchronize();
+  cudaMemcpyFromSymbol(dst, g_trace, sizeof(unsigned long long) * kTraceCtas * kTraceEvents);
+  cudaMemcpyFromSymbol(counts, g_trace_n, sizeof(unsigned int) * kTraceCtas);
+  static unsigned int zeros[kTraceCtas] = {};
+  return cuda_status(cudaMemcpyToSymbol(g_trace_n, zeros, sizeof(zeros)), "pf_trace_read");
+}
+#endif
+
 int pf_fwd_kernel_kind(int dtype, int head_dim) { return fwd_sm100_supported(dtype, head_dim) ? 1 : 0; }
 
 int pf_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int dtype, int B,

@@ -47,6 +47,25 @@ constexpr float kLn2 = 0.6931471805599453f;
 extern __device__ int g_status;
 __device__ __forceinline__ void flag_status(int bits) { atomicOr(&g_status, bits); }
 
+// Optional phase tracing for kernel development (compiled in only with
+// -DPF_TRACE): the first kTraceCtas CTAs append (clock64, event code,
+// iteration) records that pf_trace_read() returns to the host.
+#ifdef PF_TRACE
+constexpr int kTraceCtas = 64, kTraceEvents = 8192;
+extern __device__ unsigned long long g_trace[kTraceCtas * kTraceEvents];
+extern __device__ unsigned int g_trace_n[kTraceCtas];
+__device__ __forceinline__ void trace(int code, int it) {
+  if (blockIdx.x < kTraceCtas) {
+    const unsigned i = atomicAdd(&g_trace_n[blockIdx.x], 1u);
+    if (i < kTraceEvents)
+      g_trace[blockIdx.x * kTraceEvents + i] =
+          ((unsigned long long)clock64() << 20) | ((unsigned long long)(code & 0xff) << 12) | (unsigned)(it & 0xfff);
+  }
+}
+#else
+__device__ __forceinline__ void trace(int, int) {}
+#endif
+
 __device__ __forceinline__ uint64_t global_timer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -98,6 +117,32 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   for (uint32_t it = 0;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 255u) == 255u && global_timer_ns() - t0 > kWaitLimitNs) {
+      flag_status(PF_DEV_WAIT_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+// Latency-critical variant: polls with the non-suspending test_wait, so the
+// waiter resumes as soon as the phase completes (try_wait may park the thread
+// for a scheduler-chosen interval).  Same 2 s bound and status flag.
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity) {
+  if (mbar_test(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t it = 0;; ++it) {
+    if (mbar_test(bar, parity)) return true;
+    if ((it & 1023u) == 1023u && global_timer_ns() - t0 > kWaitLimitNs) {
       flag_status(PF_DEV_WAIT_TIMEOUT);
       return false;
     }
