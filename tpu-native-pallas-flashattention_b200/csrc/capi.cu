@@ -89,8 +89,9 @@ int pf_trace_read(unsigned long long* dst, unsigned int* counts) {
   cudaDeviceSynchronize();
   cudaMemcpyFromSymbol(dst, g_trace, sizeof(unsigned long long) * kTraceCtas * kTraceEvents);
   cudaMemcpyFromSymbol(counts, g_trace_n, sizeof(unsigned int) * kTraceCtas);
-  static unsigned int zeros[kTraceCtas] = {};
-  return cuda_status(cudaMemcpyToSymbol(g_trace_n, zeros, sizeof(zeros)), "pf_trace_read");
+  void* p = nullptr;
+  cudaGetSymbolAddress(&p, g_trace);
+  return cuda_status(cudaMemset(p, 0, sizeof(unsigned long long) * kTraceCtas * kTraceEvents), "pf_trace_read");
 }
 #endif
 

@@ -48,19 +48,17 @@ extern __device__ int g_status;
 __device__ __forceinline__ void flag_status(int bits) { atomicOr(&g_status, bits); }
 
 // Optional phase tracing for kernel development (compiled in only with
-// -DPF_TRACE): the first kTraceCtas CTAs append (clock64, event code,
-// iteration) records that pf_trace_read() returns to the host.
+// -DPF_TRACE): the first kTraceCtas CTAs store clock64() into fixed slots
+// [cta][event code][iteration % 512] that pf_trace_read() returns to the host
+// (plain stores, so a trace point never stalls the warp on a round trip).
 #ifdef PF_TRACE
-constexpr int kTraceCtas = 64, kTraceEvents = 8192;
+constexpr int kTraceCtas = 64, kTraceCodes = 16, kTraceIters = 512;
+constexpr int kTraceEvents = kTraceCodes * kTraceIters;
 extern __device__ unsigned long long g_trace[kTraceCtas * kTraceEvents];
 extern __device__ unsigned int g_trace_n[kTraceCtas];
 __device__ __forceinline__ void trace(int code, int it) {
-  if (blockIdx.x < kTraceCtas) {
-    const unsigned i = atomicAdd(&g_trace_n[blockIdx.x], 1u);
-    if (i < kTraceEvents)
-      g_trace[blockIdx.x * kTraceEvents + i] =
-          ((unsigned long long)clock64() << 20) | ((unsigned long long)(code & 0xff) << 12) | (unsigned)(it & 0xfff);
-  }
+  if (blockIdx.x < kTraceCtas)
+    g_trace[(blockIdx.x * kTraceCodes + (code & 15)) * kTraceIters + (it & (kTraceIters - 1))] = clock64();
 }
 #else
 __device__ __forceinline__ void trace(int, int) {}

@@ -28,9 +28,9 @@ __device__ __forceinline__ uint64_t desc_mn(uint32_t tile_addr, int kk) {
   return smem_desc_sw128(tile_addr + kk * 16 * 128, ROWS * 128, 1024);
 }
 
-// TMEM column of k-step kk of a 16-bit operand that two warpgroups packed
-// into their own 32-column halves (q or key columns [32w, 32w + 32) -> packed
-// columns [32w, 32w + 16)) of a 64-column buffer.
+// TMEM column of k-step kk (16 values of K) of a 16-bit operand packed by the
+// elementwise warps: each 32-column chunk c of an f32 tile holds its 32 values
+// as 16 packed pairs in columns [32c, 32c + 16).
 __device__ __forceinline__ uint32_t split_packed_col(int kk) {
   return (uint32_t)((kk >> 1) * 32 + (kk & 1) * 8);
 }
