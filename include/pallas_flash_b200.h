@@ -54,7 +54,8 @@ enum pf_status {
  * instead of trapping; read (and optionally clear) with pf_device_status. */
 enum pf_device_bits {
   PF_DEV_WAIT_TIMEOUT = 1, /* a bounded mbarrier wait gave up                     */
-  PF_DEV_BAD_PAGE = 2      /* a block-table entry was outside [0, num_pages)      */
+  PF_DEV_BAD_PAGE = 2,     /* a block-table entry was outside [0, num_pages)      */
+  PF_DEV_SMEM_LAYOUT = 4   /* dynamic shared memory was not 1024-byte aligned     */
 };
 
 const char* pf_last_error(void);

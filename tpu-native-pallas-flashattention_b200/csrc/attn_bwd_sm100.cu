@@ -30,14 +30,28 @@
 namespace pf {
 namespace {
 
-constexpr int kThreads = 384;  // warp 0 TMA, warp 1 MMA, warps 4-11 elementwise
+
+// Warp 0: TMA producer; warp 1: MMA issuer; warps 2 .. 2 + 4*kEWG - 1: kEWG
+// elementwise warpgroups, each owning 128/kEWG columns of a tile (a warp
+// reads TMEM lane quadrant warp % 4, so every four consecutive warps cover
+// the 128 lanes).  More elementwise warps hide more of the dependent-latency
+// chains of the P and dS steps; fewer leave more registers per thread.
+#ifndef PF_BWD_EWG
+#define PF_BWD_EWG 2
+#endif
+constexpr int kEWG = PF_BWD_EWG;
+constexpr int kNCH = 4 / kEWG;                // 32-column chunks per elementwise thread
+constexpr int kEWThreads = 128 * kEWG;
+constexpr int kThreads = 64 + kEWThreads;
 
 struct BwdBars {
   uint64_t fixed;                  // the CTA's resident tiles
-  uint64_t full[4], empty[4];      // streamed stages (dK/dV: Q+dO pairs; dQ: K ring)
-  uint64_t vfull[2], vempty[2];    // dQ: V ring
+  uint64_t full[4], empty[4];      // streamed stages (dK/dV: Q + statistics; dQ: K)
+  uint64_t vfull[4], vempty[4];    // streamed stages (dK/dV: dO; dQ: V)
   uint64_t s_full[2], dp_full;     // S / dP in TMEM
-  uint64_t p_ready, ds_ready;      // P / dS written back to TMEM
+  uint64_t p_ready, ds_ready;      // P / dS written for the accumulating MMAs
+  uint64_t pv_done;                // dK/dV: dV(it) has read the P^T tile
+  uint64_t s_free, dp_free;        // S (dK/dV) / dP (dQ) loaded into registers
   uint64_t done;                   // accumulators final
   uint32_t tmem_base;
 };
@@ -50,9 +64,13 @@ struct DkvCfg {
   static constexpr int kTile = 128 * D * 2;
   static constexpr int kFixedOff = 0;
   static constexpr int kStreamOff = 2 * kTile;
-  static constexpr int kStatOff = kStreamOff + kNS * 2 * kTile;  // [kNS][128] float2 (-lse*log2e, -delta)
-  static constexpr int kBarOff = kStatOff + kNS * 128 * 8;
-  static constexpr int kSmem = kBarOff + 256 + 1024;
+  static constexpr int kStatOff = kStreamOff + kNS * 2 * kTile;  // [kNS][2][128] f32: -lse*log2e, -delta
+  static constexpr int kPOff = kStatOff + kNS * 256 * 4;   // P^T: 128 keys x 128 queries, SW128 K-major
+  static constexpr int kBarOff = kPOff + 128 * 128 * 2;
+  // No alignment slack: at D = 128 the tiles fill the 227 KB limit, so the
+  // kernel requires (and checks) a 1024-byte aligned dynamic shared window.
+  static constexpr int kSmem = kBarOff + 256;
+  static_assert(kPOff % 1024 == 0, "P^T tile must be 1024-byte aligned");
   static constexpr uint32_t kS = 0, kDP = 128, kDV = 256, kDK = 256 + D;
 };
 
@@ -70,25 +88,58 @@ struct DqCfg {
   static constexpr uint32_t kS = 0, kDP = 256, kDQ = 384;  // S double-buffered at 0 / 128
 };
 
-// Elementwise steps shared by both kernels.  A thread owns one TMEM lane and
-// 64 columns of S / dP (two 32-column chunks at c0 and c0 + 32).
-//
-// P phase:  p = exp2(s * scale*log2e + nl2(c)) (0 where not visible), kept in
-//   f32 registers and written back packed to 16-bit pairs over the first 16
-//   columns of each chunk of the S buffer (the A operand of dV += P^T dO).
-// dS phase: ds = p * (dp + nd(c)), packed the same way over the dP buffer.
-//
-// nl2(h, c) is -lse*log2(e) and nd(h, c) is -delta for column c of chunk h (or
-// for the thread's row).  `FULL` (chosen per chunk by a warp-uniform test)
-// drops the per-element visibility selects.
-template <int FMT, bool FULL, typename Vis, typename NL2>
+// Elementwise steps on one 32-column chunk of a TMEM lane:
+//   P:  p = exp2(s * scale*log2e + nl2) (0 where not visible)
+//   dS: ds = p * (dp + nd)
+// nl2 is -lse*log2(e) and nd is -delta (per column in the dK/dV kernel, per
+// row in the dQ kernel).  `FULL` (chosen per chunk by a warp-uniform test)
+// drops the per-element visibility selects.  p stays in f32 registers; the
+// 16-bit packed P (FMT 1: bf16, 0: f16, -1: not needed) feeds an MMA.
+template <int FMT, bool FULL, typename NL2, typename Vis>
 __device__ __forceinline__ void p_chunk(const uint32_t (&rs)[32], float (&p)[32], uint32_t (&pk)[16], float2 sc2,
-                                        Vis visible, NL2 nl2) {
+                                        NL2 nl2, Vis visible);
+
+// Variant for the dK/dV kernel: p is kept as packed f16 pairs (relative
+// error 2^-12, below the 16-bit rounding of dS itself) to save registers.
+template <int FMT, bool FULL, typename NL2, typename Vis>
+__device__ __forceinline__ void p_chunk_keep16(const uint32_t (&rs)[32], uint32_t (&keep)[16], uint32_t (&pk)[16],
+                                               float2 sc2, NL2 nl2, Vis visible) {
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
     const int c = 2 * i;
-    const float2 x = fma2(make_float2(__uint_as_float(rs[c]), __uint_as_float(rs[c + 1])), sc2,
-                          nl2(c));
+    const float2 x = fma2(make_float2(__uint_as_float(rs[c]), __uint_as_float(rs[c + 1])), sc2, nl2(c));
+    float2 e = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+    if (!FULL) {
+      e.x = visible(c) ? e.x : 0.f;
+      e.y = visible(c + 1) ? e.y : 0.f;
+    }
+    keep[i] = pack_f16x2(e.x, e.y);
+    pk[i] = FMT == 1 ? pack_bf16x2(e.x, e.y) : keep[i];
+  }
+}
+
+template <int FMT, typename ND>
+__device__ __forceinline__ void ds_chunk_keep16(const uint32_t (&rd)[32], const uint32_t (&keep)[16], ND nd,
+                                                uint32_t out) {
+  uint32_t pk[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const int c = 2 * i;
+    const float2 pf = __half22float2(*reinterpret_cast<const __half2*>(&keep[i]));
+    const float2 t = add2(make_float2(__uint_as_float(rd[c]), __uint_as_float(rd[c + 1])), nd(c));
+    const float2 ds = mul2(pf, t);
+    pk[i] = FMT == 1 ? pack_bf16x2(ds.x, ds.y) : pack_f16x2(ds.x, ds.y);
+  }
+  tmem_st16(out, pk);
+}
+
+template <int FMT, bool FULL, typename NL2, typename Vis>
+__device__ __forceinline__ void p_chunk(const uint32_t (&rs)[32], float (&p)[32], uint32_t (&pk)[16], float2 sc2,
+                                        NL2 nl2, Vis visible) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const int c = 2 * i;
+    const float2 x = fma2(make_float2(__uint_as_float(rs[c]), __uint_as_float(rs[c + 1])), sc2, nl2(c));
     float2 e = make_float2(fast_exp2(x.x), fast_exp2(x.y));
     if (!FULL) {
       e.x = visible(c) ? e.x : 0.f;
@@ -96,47 +147,54 @@ __device__ __forceinline__ void p_chunk(const uint32_t (&rs)[32], float (&p)[32]
     }
     p[c] = e.x;
     p[c + 1] = e.y;
-    pk[i] = FMT == 1 ? pack_bf16x2(e.x, e.y) : pack_f16x2(e.x, e.y);
+    if (FMT >= 0) pk[i] = FMT == 1 ? pack_bf16x2(e.x, e.y) : pack_f16x2(e.x, e.y);
   }
 }
 
-template <int FMT, typename Vis, typename Full, typename NL2>
-__device__ __forceinline__ void p_phase(uint32_t s_addr, float scale_log2, Full full, Vis visible, NL2 nl2,
-                                        float (&p)[2][32]) {
-  uint32_t rs[2][32];
-  tmem_ld32(s_addr, rs[0]);
-  tmem_ld32(s_addr + 32, rs[1]);
-  tmem_wait_ld();
-  const float2 sc2 = make_float2(scale_log2, scale_log2);
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    uint32_t pk[16];
-    auto vis_h = [&](int c) { return visible(h, c); };
-    auto nl2_h = [&](int c) { return nl2(h, c); };
-    if (full(h)) p_chunk<FMT, true>(rs[h], p[h], pk, sc2, vis_h, nl2_h);
-    else p_chunk<FMT, false>(rs[h], p[h], pk, sc2, vis_h, nl2_h);
-    tmem_st16(s_addr + 32 * h, pk);
-  }
-}
-
+// dS of one chunk from dP in registers, packed over the first 16 columns of
+// the chunk at TMEM address `out` (the A operand of the dK / dQ MMA).
 template <int FMT, typename ND>
-__device__ __forceinline__ void ds_phase(uint32_t dp_addr, ND nd, const float (&p)[2][32]) {
-  uint32_t rd[2][32];
-  tmem_ld32(dp_addr, rd[0]);
-  tmem_ld32(dp_addr + 32, rd[1]);
-  tmem_wait_ld();
+__device__ __forceinline__ void ds_chunk(const uint32_t (&rd)[32], const float (&p)[32], ND nd, uint32_t out) {
+  uint32_t pk[16];
 #pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    uint32_t pk[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const int c = 2 * i;
-      const float2 t = add2(make_float2(__uint_as_float(rd[h][c]), __uint_as_float(rd[h][c + 1])), nd(h, c));
-      const float2 ds = mul2(make_float2(p[h][c], p[h][c + 1]), t);
-      pk[i] = FMT == 1 ? pack_bf16x2(ds.x, ds.y) : pack_f16x2(ds.x, ds.y);
-    }
-    tmem_st16(dp_addr + 32 * h, pk);
+  for (int i = 0; i < 16; ++i) {
+    const int c = 2 * i;
+    const float2 t = add2(make_float2(__uint_as_float(rd[c]), __uint_as_float(rd[c + 1])), nd(c));
+    const float2 ds = mul2(make_float2(p[c], p[c + 1]), t);
+    pk[i] = FMT == 1 ? pack_bf16x2(ds.x, ds.y) : pack_f16x2(ds.x, ds.y);
   }
+  tmem_st16(out, pk);
+}
+
+// N consecutive floats of a shared-memory array into registers.
+template <int N>
+__device__ __forceinline__ void load_cols(const float* src, float (&dst)[N]) {
+  const float4* s4 = reinterpret_cast<const float4*>(src);
+#pragma unroll
+  for (int i = 0; i < N / 4; ++i) {
+    const float4 v = s4[i];
+    dst[4 * i] = v.x;
+    dst[4 * i + 1] = v.y;
+    dst[4 * i + 2] = v.z;
+    dst[4 * i + 3] = v.w;
+  }
+}
+
+// Packed P for columns [col0, col0 + 32*NCH) of key row `r` into the P^T tile
+// (two 128-byte-swizzled K-major boxes of 64 columns): 16-byte chunk j of a
+// box row lives at chunk position j ^ (r % 8).
+template <int NCH>
+__device__ __forceinline__ void store_sw128_cols(uint8_t* tile, int r, int col0, const uint32_t (&pk)[NCH][16]) {
+  uint8_t* row = tile + (col0 / 64) * (128 * 128) + r * 128;
+  const int j0 = (col0 % 64) / 8;
+#pragma unroll
+  for (int h = 0; h < NCH; ++h)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int j = j0 + 4 * h + q;
+      *reinterpret_cast<uint4*>(row + ((j ^ (r & 7)) << 4)) =
+          make_uint4(pk[h][4 * q], pk[h][4 * q + 1], pk[h][4 * q + 2], pk[h][4 * q + 3]);
+    }
 }
 
 // Writes an f32 accumulator row (TMEM columns [col0, col0 + n)) times `scale`
@@ -182,7 +240,11 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
   constexpr uint32_t idesc_acc = make_idesc_f16(FMT, 128, D, 0, 1);
 
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  if (smem_u32(smem_raw) & 1023) {  // uniform over the CTA: nothing initialised yet
+    if (threadIdx.x == 0) flag_status(PF_DEV_SMEM_LAYOUT);
+    return;
+  }
+  uint8_t* smem = smem_raw;
   BwdBars* bars = reinterpret_cast<BwdBars*>(smem + Cfg::kBarOff);
   const uint32_t sbase = smem_u32(smem);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -205,11 +267,15 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
     for (int s = 0; s < NS; ++s) {
       mbar_init(&bars->full[s], 1 + 32);  // TMA tx arrive + the producer warp's 32 stat writers
       mbar_init(&bars->empty[s], 1);
+      mbar_init(&bars->vfull[s], 1);
+      mbar_init(&bars->vempty[s], 1);
     }
     mbar_init(&bars->s_full[0], 1);
     mbar_init(&bars->dp_full, 1);
-    mbar_init(&bars->p_ready, 256);
-    mbar_init(&bars->ds_ready, 256);
+    mbar_init(&bars->p_ready, kEWThreads);
+    mbar_init(&bars->ds_ready, kEWThreads);
+    mbar_init(&bars->pv_done, 1);
+    mbar_init(&bars->s_free, kEWThreads);
     mbar_init(&bars->done, 1);
     fence_barrier_init();
   }
@@ -221,7 +287,7 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
-  float2* stats = reinterpret_cast<float2*>(smem + Cfg::kStatOff);
+  float* stats = reinterpret_cast<float*>(smem + Cfg::kStatOff);
 
   if (warp == 0) {
     if (n_it > 0) {
@@ -236,152 +302,224 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
                       kv_plane);
         }
       }
-      for (int it = 0; it < n_it; ++it) {
-        const int s = it % NS;
-        if (it >= NS && !mbar_wait(&bars->empty[s], ((it / NS) - 1) & 1)) break;
-        const int g = it / nqi, qi = i0 + it % nqi;
-        const int plane = b * H + hk * G + g;
-        if (lane == 0) {
-          uint8_t* qdst = smem + Cfg::kStreamOff + s * 2 * Cfg::kTile;
-          mbar_expect_tx(&bars->full[s], 2 * Cfg::kTile);
-          for (int c = 0; c < Cfg::kBoxes; ++c) {
-            tma_load_3d(qdst + c * 128 * 128, &tm_q, &bars->full[s], c * 64, qi * 128, plane);
-            tma_load_3d(qdst + Cfg::kTile + c * 128 * 128, &tm_do, &bars->full[s], c * 64, qi * 128, plane);
-          }
-        }
+      // Column statistics are fetched one tile ahead, so their global-load
+      // latency stays off the Q barrier.
+      float pl[4], pd[4];
+      auto fetch_stats = [&](int it) {
+        const int plane = b * H + hk * G + it / nqi;
+        const int qi = i0 + it % nqi;
         const long srow = (long)plane * Sq;
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          const int c = lane + 32 * u, qp = qi * 128 + c;
-          stats[s * 128 + c] = qp < Sq ? make_float2(-lse[srow + qp] * kLog2e, -delta[srow + qp])
-                                       : make_float2(0.f, 0.f);
+          const int qp = qi * 128 + lane + 32 * u;
+          pl[u] = qp < Sq ? -lse[srow + qp] * kLog2e : 0.f;
+          pd[u] = qp < Sq ? -delta[srow + qp] : 0.f;
+        }
+      };
+      fetch_stats(0);
+      for (int it = 0; it < n_it; ++it) {
+        const int s = it % NS;
+        if (it >= NS && !mbar_wait(&bars->empty[s], ((it / NS) - 1) & 1)) break;
+        if (lane == 0) trace(15, it - 1);
+        const int g = it / nqi, qi = i0 + it % nqi;
+        const int plane = b * H + hk * G + g;
+        uint8_t* qdst = smem + Cfg::kStreamOff + s * 2 * Cfg::kTile;
+        if (lane == 0) {
+          mbar_expect_tx(&bars->full[s], Cfg::kTile);
+          for (int c = 0; c < Cfg::kBoxes; ++c)
+            tma_load_3d(qdst + c * 128 * 128, &tm_q, &bars->full[s], c * 64, qi * 128, plane);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          stats[s * 256 + lane + 32 * u] = pl[u];
+          stats[s * 256 + 128 + lane + 32 * u] = pd[u];
         }
         mbar_arrive(&bars->full[s]);
+        if (it + 1 < n_it) fetch_stats(it + 1);
+        // dO is needed later (by dP) and released earlier (after dV) than Q.
+        if (it >= NS && !mbar_wait(&bars->vempty[s], ((it / NS) - 1) & 1)) break;
+        if (lane == 0) {
+          mbar_expect_tx(&bars->vfull[s], Cfg::kTile);
+          for (int c = 0; c < Cfg::kBoxes; ++c)
+            tma_load_3d(qdst + Cfg::kTile + c * 128 * 128, &tm_do, &bars->vfull[s], c * 64, qi * 128, plane);
+        }
       }
     }
   } else if (warp == 1) {
-    // Tensor-core order per iteration:  dV(it) [P ready]  S(it+1)  dK(it) [dS ready]  dP(it+1).
-    // The P phase of it+1 overlaps dK(it) and dP(it+1); the dS phase of it
-    // overlaps dV(it) and S(it+1).  In-order execution makes S(it+1) overwrite
-    // P(it) only after dV(it) read it, and dP(it+1) overwrite dS(it) after dK(it).
+    // Tensor-core order per iteration:
+    //   [S(it) in registers] S(it+1)   [P(it) in smem] dV(it)   [dS(it) in TMEM] dK(it) dP(it+1)
+    // The elementwise warps release the S tile as soon as they have loaded
+    // it and write P^T to shared memory, so S(it+1) runs under the P
+    // arithmetic of tile it and the tensor core always has queued work (a
+    // burst issued to an idle tensor core pays several hundred cycles of
+    // latency).  dS stays in TMEM; dP(it+1) overwrites it only after dK(it)
+    // read it (the tensor core runs its queue in order).
     if (lane == 0 && n_it > 0) {
       bool ok = mbar_wait(&bars->fixed, 0);
       tc_fence_after();
       const uint32_t k_addr = sbase + Cfg::kFixedOff, v_addr = k_addr + Cfg::kTile;
+      const uint64_t kd = desc_k_base<128>(k_addr), vd = desc_k_base<128>(v_addr);
+      const uint64_t pd = desc_k_base<128>(sbase + Cfg::kPOff);
       auto stage = [&](int it) { return sbase + Cfg::kStreamOff + (it % NS) * 2 * Cfg::kTile; };
       auto issue_s = [&](int it) {
         const uint32_t q_addr = stage(it);
+        const uint64_t qd = desc_k_base<128>(q_addr);
+        umma_ss(tmem + Cfg::kS, kd, qd, idesc_s, 0);
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk)
-          umma_ss(tmem + Cfg::kS, desc_k<128>(k_addr, kk), desc_k<128>(q_addr, kk), idesc_s, kk > 0);
+        for (int kk = 1; kk < D / 16; ++kk)
+          umma_ss_acc(tmem + Cfg::kS, kd + koff<128>(kk), qd + koff<128>(kk), idesc_s);
         umma_commit(&bars->s_full[0]);
       };
-      auto issue_dp = [&](int it) {
+      auto issue_dp = [&](int it) -> bool {
+        if (!mbar_wait_spin(&bars->vfull[it % NS], (it / NS) & 1)) return false;
+        tc_fence_after();
         const uint32_t do_addr = stage(it) + Cfg::kTile;
+        const uint64_t od = desc_k_base<128>(do_addr);
+        umma_ss(tmem + Cfg::kDP, vd, od, idesc_s, 0);
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk)
-          umma_ss(tmem + Cfg::kDP, desc_k<128>(v_addr, kk), desc_k<128>(do_addr, kk), idesc_s, kk > 0);
+        for (int kk = 1; kk < D / 16; ++kk)
+          umma_ss_acc(tmem + Cfg::kDP, vd + koff<128>(kk), od + koff<128>(kk), idesc_s);
         umma_commit(&bars->dp_full);
+        return true;
       };
       if (ok) ok = mbar_wait_spin(&bars->full[0], 0);
       if (ok) {
         tc_fence_after();
         issue_s(0);
-        issue_dp(0);
+        ok = issue_dp(0);
       }
       for (int it = 0; ok && it < n_it; ++it) {
         const uint32_t q_addr = stage(it), do_addr = q_addr + Cfg::kTile;
-        ok = mbar_wait_spin(&bars->p_ready, it & 1);
-        if (!ok) break;
-        trace(1, it);
-        tc_fence_after();
+        // S(it+1) and dV(it) are independent; issue whichever is ready first
+        // so a late Q tile does not hold back dV (bounded like every wait).
+        bool need_s = it + 1 < n_it, need_v = true;
+        const uint64_t t0 = global_timer_ns();
+        for (uint32_t spin = 1; ok && (need_s || need_v); ++spin) {
+          if (need_s && mbar_test(&bars->s_free, it & 1) &&
+              mbar_test(&bars->full[(it + 1) % NS], ((it + 1) / NS) & 1)) {
+            trace(14, it);
+            tc_fence_after();
+            issue_s(it + 1);
+            need_s = false;
+          } else if (need_v && mbar_test(&bars->p_ready, it & 1)) {
+            trace(1, it);
+            tc_fence_after();
+            const uint64_t om = desc_mn_base<128>(do_addr);
+            umma_ss(tmem + Cfg::kDV, pd, om, idesc_acc, it > 0);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          umma_ts(tmem + Cfg::kDV, tmem + Cfg::kS + split_packed_col(kk), desc_mn<128>(do_addr, kk), idesc_acc,
-                  (it > 0 || kk > 0));
-        if (it + 1 < n_it) {
-          ok = mbar_wait_spin(&bars->full[(it + 1) % NS], ((it + 1) / NS) & 1);
-          if (!ok) break;
-          tc_fence_after();
-          issue_s(it + 1);
+            for (int kk = 1; kk < 8; ++kk)
+              umma_ss_acc(tmem + Cfg::kDV, pd + koff<128>(kk), om + mnoff(kk), idesc_acc);
+            umma_commit(&bars->pv_done);
+            umma_commit(&bars->vempty[it % NS]);
+            need_v = false;
+          } else if ((spin & 1023u) == 0 && global_timer_ns() - t0 > kWaitLimitNs) {
+            flag_status(PF_DEV_WAIT_TIMEOUT);
+            ok = false;
+          }
         }
+        if (!ok) break;
         trace(2, it);
         ok = mbar_wait_spin(&bars->ds_ready, it & 1);
         if (!ok) break;
         trace(3, it);
         tc_fence_after();
+        const uint64_t qm = desc_mn_base<128>(q_addr);
+        umma_ts(tmem + Cfg::kDK, tmem + Cfg::kDP, qm, idesc_acc, it > 0);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          umma_ts(tmem + Cfg::kDK, tmem + Cfg::kDP + split_packed_col(kk), desc_mn<128>(q_addr, kk), idesc_acc,
-                  (it > 0 || kk > 0));
+        for (int kk = 1; kk < 8; ++kk)
+          umma_ts_acc(tmem + Cfg::kDK, tmem + Cfg::kDP + split_packed_col(kk), qm + mnoff(kk), idesc_acc);
         umma_commit(&bars->empty[it % NS]);
-        if (it + 1 < n_it) issue_dp(it + 1);
+        if (it + 1 < n_it && !(ok = issue_dp(it + 1))) break;
         trace(4, it);
       }
       umma_commit(&bars->done);
     }
-  } else if (warp >= 4) {
-    const int w = (warp - 4) / 4;  // query columns [64w, 64w + 64) of each tile
+  } else if (warp >= 2) {
+    const int cw = (warp - 2) / 4;      // elementwise warpgroup
+    const int col0 = 32 * kNCH * cw;    // its first query column of the tile
     const int quad = warp % 4;
-    const int row = quad * 32 + lane;  // key row within the tile
+    const int row = quad * 32 + lane;   // key row within the tile
     const int kpos = k0 + row;
     const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
     const bool key_ok = kpos < kv_len;
+    const bool tr = lane == 0 && quad == 2 && cw < 2;  // trace writers
+    const float2 sc2 = make_float2(scale_log2, scale_log2);
     bool ok = true;
-    float p[2][32];
     for (int it = 0; ok && it < n_it; ++it) {
       const int st = it % NS;
-      const int qc = (i0 + it % nqi) * 128 + 64 * w;  // first query column of this thread's half
+      const int qc = (i0 + it % nqi) * 128 + col0;  // first query column of this thread
       // The stage's statistics were written by the producer warp before its
       // arrive on full[st]; the stage is not refilled before dK(it) retires.
-      if (!mbar_wait_spin(&bars->s_full[0], it & 1) || !mbar_wait(&bars->full[st], (it / NS) & 1)) {
-        ok = false;
-        break;
-      }
-      if (threadIdx.x == 128 || threadIdx.x == 256) trace(8 + 2 * w, it);
+      // Loading them before the S wait keeps their latency off the critical path.
+      if (!mbar_wait(&bars->full[st], (it / NS) & 1)) { ok = false; break; }
+      float nl2[kNCH * 32];
+      load_cols<kNCH * 32>(stats + st * 256 + col0, nl2);
+      if (!mbar_wait_spin(&bars->s_full[0], it & 1)) { ok = false; break; }
+      if (tr) trace(8 + 3 * cw, it);
       tc_fence_after();
-      const float4* st4 = reinterpret_cast<const float4*>(stats + st * 128 + 64 * w);
-      p_phase<FMT>(
-          lane_base + Cfg::kS + 64 * w, scale_log2,
-          [&](int h) {
-            const int q0 = qc + 32 * h;
-            return (k0 + 127 < kv_len) && (q0 + 32 <= Sq) && (!causal || q0 >= k0 + 127);
-          },
-          [&](int h, int c) {
-            const int qp = qc + 32 * h + c;
-            return key_ok && qp < Sq && (!causal || qp >= kpos);
-          },
-          [&](int h, int c) {
-            const float4 v4 = st4[16 * h + c / 2];
-            return make_float2(v4.x, v4.z);
-          },
-          p);
-      tmem_wait_st();
+      uint32_t keep[kNCH][16], pk[kNCH][16];
+      {
+        uint32_t rs[kNCH][32];
+#pragma unroll
+        for (int h = 0; h < kNCH; ++h) tmem_ld32(lane_base + Cfg::kS + col0 + 32 * h, rs[h]);
+        tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(&bars->s_free);  // S(it+1) may now overwrite the tile
+        if (tr && cw == 0) trace(5, it);
+#pragma unroll
+        for (int h = 0; h < kNCH; ++h) {
+          const int q0 = qc + 32 * h;
+          auto nl2_h = [&](int c) { return make_float2(nl2[32 * h + c], nl2[32 * h + c + 1]); };
+          if ((k0 + 127 < kv_len) && (q0 + 32 <= Sq) && (!causal || q0 >= k0 + 127)) {
+            p_chunk_keep16<FMT, true>(rs[h], keep[h], pk[h], sc2, nl2_h, [](int) { return true; });
+          } else {
+            p_chunk_keep16<FMT, false>(rs[h], keep[h], pk[h], sc2, nl2_h, [&](int c) {
+              const int qp = q0 + c;
+              return key_ok && qp < Sq && (!causal || qp >= kpos);
+            });
+          }
+        }
+        if (tr && cw == 0) trace(6, it);
+      }
+      // The P^T tile is single-buffered: dV(it-1) must have read it.
+      if (it > 0 && !mbar_wait_spin(&bars->pv_done, (it - 1) & 1)) { ok = false; break; }
+      store_sw128_cols<kNCH>(smem + Cfg::kPOff, row, col0, pk);
+      fence_proxy_async_smem();
+      if (tr && cw == 0) trace(7, it);
       tc_fence_before();
       mbar_arrive(&bars->p_ready);
-      if (threadIdx.x == 128 || threadIdx.x == 256) trace(9 + 2 * w, it);
+      float nd[kNCH * 32];
+      load_cols<kNCH * 32>(stats + st * 256 + 128 + col0, nd);
+      if (tr) trace(9 + 3 * cw, it);
       if (!mbar_wait_spin(&bars->dp_full, it & 1)) { ok = false; break; }
       tc_fence_after();
-      ds_phase<FMT>(lane_base + Cfg::kDP + 64 * w,
-                    [&](int h, int c) {
-                      const float4 v4 = st4[16 * h + c / 2];
-                      return make_float2(v4.y, v4.w);
-                    },
-                    p);
+#pragma unroll
+      for (int h = 0; h < kNCH; ++h) {
+        uint32_t rd[32];
+        tmem_ld32(lane_base + Cfg::kDP + col0 + 32 * h, rd);
+        tmem_wait_ld();
+        ds_chunk_keep16<FMT>(rd, keep[h], [&](int c) { return make_float2(nd[32 * h + c], nd[32 * h + c + 1]); },
+                             lane_base + Cfg::kDP + col0 + 32 * h);
+      }
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&bars->ds_ready);
-      if (threadIdx.x == 128 || threadIdx.x == 256) trace(10 + 2 * w, it);
+      if (tr) trace(10 + 3 * cw, it);
     }
-    // Epilogue: warpgroup 0 writes dV, warpgroup 1 writes dK (scaled).
+    // Epilogue: the first half of the warpgroups writes dV, the second half
+    // dK (scaled), each a contiguous slice of the D columns.
     const bool have = n_it > 0 && ok && mbar_wait(&bars->done, 0);
     if (n_it > 0) tc_fence_after();
     const bool write = kpos < Sk;
     const long orow = ((long)(b * Hkv + hk) * Sk + kpos) * D;
-    if (w == 0)
-      store_acc_row<T, FMT>(lane_base + Cfg::kDV, dv + orow, D, 1.f, !have, write);
+    constexpr int kHalf = kEWG / 2, kCols = D / kHalf;
+    const int part = cw % kHalf;
+    if (cw < kHalf)
+      store_acc_row<T, FMT>(lane_base + Cfg::kDV + part * kCols, dv + orow + part * kCols, kCols, 1.f, !have,
+                            write);
     else
-      store_acc_row<T, FMT>(lane_base + Cfg::kDK, dk + orow, D, sm_scale, !have, write);
+      store_acc_row<T, FMT>(lane_base + Cfg::kDK + part * kCols, dk + orow + part * kCols, kCols, sm_scale,
+                            !have, write);
   }
 
   tc_fence_before();
@@ -439,7 +577,8 @@ bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     mbar_init(&bars->s_full[0], 1);
     mbar_init(&bars->s_full[1], 1);
     mbar_init(&bars->dp_full, 1);
-    mbar_init(&bars->ds_ready, 256);
+    mbar_init(&bars->dp_free, kEWThreads);
+    mbar_init(&bars->ds_ready, kEWThreads);
     mbar_init(&bars->done, 1);
     fence_barrier_init();
   }
@@ -475,22 +614,27 @@ bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       }
     }
   } else if (warp == 1) {
-    // Tensor-core order per iteration:  S(it+1)  dQ(it) [dS ready]  dP(it+1).
-    // S is double-buffered, so S(it+1) runs while the elementwise warps still
-    // work on tile it; dP(it+1) overwrites dS(it) only after dQ(it) read it.
+    // Tensor-core order per iteration:
+    //   [dP(it) in registers] dP(it+1)   [dS(it) in TMEM] dQ(it) S(it+2)
+    // S is double-buffered and dS(it) is written over the consumed S(it)
+    // tile, so the dP buffer is free as soon as the elementwise warps have
+    // loaded dP(it): dP(it+1) runs under the dS arithmetic of tile it, and
+    // S(it+2) (same buffer as S(it)) queues behind dQ(it), which reads dS(it).
     if (lane == 0 && n_it > 0) {
       bool ok = mbar_wait(&bars->fixed, 0);
       tc_fence_after();
       const uint32_t q_addr = sbase + Cfg::kFixedOff, do_addr = q_addr + Cfg::kTile;
+      const uint64_t qd = desc_k_base<128>(q_addr), od = desc_k_base<128>(do_addr);
       auto k_tile = [&](int it) { return sbase + Cfg::kKOff + (it % NK) * Cfg::kTile; };
       auto issue_s = [&](int it) -> bool {
         if (!mbar_wait_spin(&bars->full[it % NK], (it / NK) & 1)) return false;
         tc_fence_after();
         const uint32_t k_addr = k_tile(it);
+        const uint64_t kdesc = desc_k_base<128>(k_addr);
+        const uint32_t dst = tmem + Cfg::kS + 128 * (it & 1);
+        umma_ss(dst, qd, kdesc, idesc_s, 0);
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk)
-          umma_ss(tmem + Cfg::kS + 128 * (it & 1), desc_k<128>(q_addr, kk), desc_k<128>(k_addr, kk), idesc_s,
-                  kk > 0);
+        for (int kk = 1; kk < D / 16; ++kk) umma_ss_acc(dst, qd + koff<128>(kk), kdesc + koff<128>(kk), idesc_s);
         umma_commit(&bars->s_full[it & 1]);
         return true;
       };
@@ -498,70 +642,105 @@ bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         if (!mbar_wait_spin(&bars->vfull[it % NV], (it / NV) & 1)) return false;
         tc_fence_after();
         const uint32_t v_addr = sbase + Cfg::kVOff + (it % NV) * Cfg::kTile;
+        const uint64_t vdesc = desc_k_base<128>(v_addr);
+        umma_ss(tmem + Cfg::kDP, od, vdesc, idesc_s, 0);
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk)
-          umma_ss(tmem + Cfg::kDP, desc_k<128>(do_addr, kk), desc_k<128>(v_addr, kk), idesc_s, kk > 0);
+        for (int kk = 1; kk < D / 16; ++kk)
+          umma_ss_acc(tmem + Cfg::kDP, od + koff<128>(kk), vdesc + koff<128>(kk), idesc_s);
         umma_commit(&bars->vempty[it % NV]);
         umma_commit(&bars->dp_full);
         return true;
       };
-      if (ok) ok = issue_s(0) && issue_dp(0);
+      if (ok) ok = issue_s(0) && (n_it < 2 || issue_s(1)) && issue_dp(0);
       for (int it = 0; ok && it < n_it; ++it) {
-        if (it + 1 < n_it && !(ok = issue_s(it + 1))) break;
+        if (it + 1 < n_it) {
+          if (!(ok = mbar_wait_spin(&bars->dp_free, it & 1))) break;
+          tc_fence_after();
+          if (!(ok = issue_dp(it + 1))) break;
+        }
         trace(2, it);
         ok = mbar_wait_spin(&bars->ds_ready, it & 1);
         if (!ok) break;
         trace(3, it);
         tc_fence_after();
         const uint32_t k_addr = k_tile(it);
+        const uint32_t ds_addr = tmem + Cfg::kS + 128 * (it & 1);
+        const uint64_t km = desc_mn_base<128>(k_addr);
+        umma_ts(tmem + Cfg::kDQ, ds_addr, km, idesc_acc, it > 0);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          umma_ts(tmem + Cfg::kDQ, tmem + Cfg::kDP + split_packed_col(kk), desc_mn<128>(k_addr, kk), idesc_acc,
-                  (it > 0 || kk > 0));
+        for (int kk = 1; kk < 8; ++kk)
+          umma_ts_acc(tmem + Cfg::kDQ, ds_addr + split_packed_col(kk), km + mnoff(kk), idesc_acc);
         umma_commit(&bars->empty[it % NK]);
-        if (it + 1 < n_it && !(ok = issue_dp(it + 1))) break;
+        if (it + 2 < n_it && !(ok = issue_s(it + 2))) break;
         trace(4, it);
       }
       umma_commit(&bars->done);
     }
-  } else if (warp >= 4) {
-    const int w = (warp - 4) / 4;  // key columns [64w, 64w + 64) of each tile
+  } else if (warp >= 2) {
+    const int cw = (warp - 2) / 4;      // elementwise warpgroup
+    const int col0 = 32 * kNCH * cw;    // its first key column of the tile
     const int quad = warp % 4;
-    const int row = quad * 32 + lane;  // query row within the tile
+    const int row = quad * 32 + lane;   // query row within the tile
     const int qpos = q0 + row;
     const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
     const long srow = (long)bh * Sq + qpos;
     const float nl2 = qpos < Sq ? -lse[srow] * kLog2e : 0.f;
     const float nd = qpos < Sq ? -delta[srow] : 0.f;
+    const bool tr = lane == 0 && quad == 2 && cw < 2;
     bool ok = true;
-    float p[2][32];
+    const float2 sc2 = make_float2(scale_log2, scale_log2);
+    const float2 nl2v = make_float2(nl2, nl2), ndv = make_float2(nd, nd);
     for (int it = 0; it < n_it; ++it) {
       if (!mbar_wait_spin(&bars->s_full[it & 1], (it >> 1) & 1)) { ok = false; break; }
-      if (threadIdx.x == 128 || threadIdx.x == 256) trace(8 + 2 * w, it);
+      if (tr) trace(8 + 3 * cw, it);
       tc_fence_after();
-      const int kc = it * 128 + 64 * w;  // first key column of this thread's half
-      p_phase<FMT>(
-          lane_base + Cfg::kS + 128 * (it & 1) + 64 * w, scale_log2,
-          [&](int hh) { const int kb = kc + 32 * hh; return (kb + 32 <= kv_len) && (!causal || kb + 31 <= q0); },
-          [&](int hh, int c) {
-            const int kp = kc + 32 * hh + c;
-            return kp < kv_len && (!causal || kp <= qpos);
-          },
-          [&](int, int) { return make_float2(nl2, nl2); }, p);
-      if (threadIdx.x == 128 || threadIdx.x == 256) trace(9 + 2 * w, it);
+      const uint32_t s_addr = lane_base + Cfg::kS + 128 * (it & 1) + col0;
+      const int kc = it * 128 + col0;  // first key column of this thread
+      float p[kNCH][32];
+      {
+        uint32_t rs[kNCH][32];
+        uint32_t unused[16];
+#pragma unroll
+        for (int h = 0; h < kNCH; ++h) tmem_ld32(s_addr + 32 * h, rs[h]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int h = 0; h < kNCH; ++h) {
+          const int kb = kc + 32 * h;
+          if ((kb + 32 <= kv_len) && (!causal || kb + 31 <= q0)) {
+            p_chunk<-1, true>(rs[h], p[h], unused, sc2, [&](int) { return nl2v; }, [](int) { return true; });
+          } else {
+            p_chunk<-1, false>(rs[h], p[h], unused, sc2, [&](int) { return nl2v; }, [&](int c) {
+              const int kp = kb + c;
+              return kp < kv_len && (!causal || kp <= qpos);
+            });
+          }
+        }
+      }
+      if (tr) trace(9 + 3 * cw, it);
       if (!mbar_wait_spin(&bars->dp_full, it & 1)) { ok = false; break; }
       tc_fence_after();
-      ds_phase<FMT>(lane_base + Cfg::kDP + 64 * w, [&](int, int) { return make_float2(nd, nd); }, p);
+      {
+        uint32_t rd[kNCH][32];
+#pragma unroll
+        for (int h = 0; h < kNCH; ++h) tmem_ld32(lane_base + Cfg::kDP + col0 + 32 * h, rd[h]);
+        tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(&bars->dp_free);  // dP(it+1) may now overwrite the tile
+#pragma unroll
+        for (int h = 0; h < kNCH; ++h)
+          ds_chunk<FMT>(rd[h], p[h], [&](int) { return ndv; }, s_addr + 32 * h);
+      }
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&bars->ds_ready);
-      if (threadIdx.x == 128 || threadIdx.x == 256) trace(10 + 2 * w, it);
+      if (tr) trace(10 + 3 * cw, it);
     }
     const bool have = n_it > 0 && ok && mbar_wait(&bars->done, 0);
     if (n_it > 0) tc_fence_after();
-    // Each warpgroup writes half of the D columns of its rows.
-    store_acc_row<T, FMT>(lane_base + Cfg::kDQ + w * (D / 2), dq + srow * D + w * (D / 2), D / 2, sm_scale,
-                          !have, qpos < Sq);
+    // The first two warpgroups write half of the D columns of their rows each.
+    if (cw < 2)
+      store_acc_row<T, FMT>(lane_base + Cfg::kDQ + cw * (D / 2), dq + srow * D + cw * (D / 2), D / 2, sm_scale,
+                            !have, qpos < Sq);
   }
 
   tc_fence_before();

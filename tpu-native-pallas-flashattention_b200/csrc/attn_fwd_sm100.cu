@@ -229,23 +229,26 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         ok = mbar_wait(&bars->q, 0);
       }
       tc_fence_after();
-      const uint32_t q_addr[2] = {sbase + Cfg::kQOff, sbase + Cfg::kQOff + Cfg::kTileBytes};
+      // Descriptors are built once per tile; each k-step adds a constant.
+      const uint64_t q_desc[2] = {desc_k_base<kBM>(sbase + Cfg::kQOff),
+                                  desc_k_base<kBM>(sbase + Cfg::kQOff + Cfg::kTileBytes)};
       const uint32_t s_col[2] = {Cfg::kS0, Cfg::kS1};
       const uint32_t o_col[2] = {Cfg::kO0, Cfg::kO1};
       auto issue_s = [&](int w, int j) {
-        const uint32_t k_addr = sbase + Cfg::kKOff + (j % KS) * Cfg::kTileBytes;
+        const uint64_t kd = desc_k_base<kBN>(sbase + Cfg::kKOff + (j % KS) * Cfg::kTileBytes);
+        const uint64_t qd = q_desc[w];
+        const uint32_t dst = tmem + s_col[w];
+        umma_ss(dst, qd, kd, idesc_qk, 0u);
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk)
-          umma_ss(tmem + s_col[w], desc_k<kBM>(q_addr[w], kk), desc_k<kBN>(k_addr, kk),
-                  idesc_qk, kk > 0 ? 1u : 0u);
+        for (int kk = 1; kk < D / 16; ++kk) umma_ss_acc(dst, qd + koff<kBM>(kk), kd + koff<kBN>(kk), idesc_qk);
         umma_commit(&bars->s_full[w]);
       };
       auto issue_pv = [&](int w, int j) {
-        const uint32_t v_addr = sbase + Cfg::kVOff + (j % VS) * Cfg::kTileBytes;
+        const uint64_t vd = desc_mn_base<kBN>(sbase + Cfg::kVOff + (j % VS) * Cfg::kTileBytes);
+        const uint32_t dst = tmem + o_col[w], src = tmem + s_col[w];
+        umma_ts(dst, src, vd, idesc_pv, j > 0 ? 1u : 0u);
 #pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk)
-          umma_ts(tmem + o_col[w], tmem + s_col[w] + kk * 8, desc_mn<kBN>(v_addr, kk), idesc_pv,
-                  (j > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 1; kk < kBN / 16; ++kk) umma_ts_acc(dst, src + kk * 8, vd + mnoff(kk), idesc_pv);
         umma_commit(&bars->o_done[w]);
       };
       for (int j = 0; ok && j <= n_max; ++j) {

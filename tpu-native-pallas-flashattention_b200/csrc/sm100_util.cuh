@@ -28,6 +28,26 @@ __device__ __forceinline__ uint64_t desc_mn(uint32_t tile_addr, int kk) {
   return smem_desc_sw128(tile_addr + kk * 16 * 128, ROWS * 128, 1024);
 }
 
+// Cheap per-MMA descriptors: the start-address field is linear (address/16 in
+// bits 0-13, and shared addresses stay below 256 KB, so it never carries), so
+// the descriptor of k-step kk is the tile's base descriptor plus a
+// compile-time constant.  The MMA-issuing thread shares its scheduler with
+// busy elementwise warps; every instruction it spends between two MMAs
+// delays the tensor core, so descriptors are built once per tile.
+template <int ROWS>
+__device__ __forceinline__ uint64_t desc_k_base(uint32_t tile_addr) {
+  return smem_desc_sw128(tile_addr, 16, 1024);
+}
+template <int ROWS>
+__device__ __forceinline__ uint64_t desc_mn_base(uint32_t tile_addr) {
+  return smem_desc_sw128(tile_addr, ROWS * 128, 1024);
+}
+template <int ROWS>
+constexpr uint64_t koff(int kk) {
+  return (uint64_t)(((kk >> 2) * (ROWS * 128) + (kk & 3) * 32) >> 4);
+}
+constexpr uint64_t mnoff(int kk) { return (uint64_t)(kk * 16 * 128 >> 4); }
+
 // TMEM column of k-step kk (16 values of K) of a 16-bit operand packed by the
 // elementwise warps: each 32-column chunk c of an f32 tile holds its 32 values
 // as 16 packed pairs in columns [32c, 32c + 16).

@@ -26,6 +26,7 @@ PF_ERR_WORKSPACE = 5
 
 PF_DEV_WAIT_TIMEOUT = 1
 PF_DEV_BAD_PAGE = 2
+PF_DEV_SMEM_LAYOUT = 4
 
 _DTYPES = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
 
