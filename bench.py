@@ -88,7 +88,10 @@ class ClockSampler:
                  "hw_thermal_slowdown": nv.nvmlClocksEventReasonHwThermalSlowdown,
                  "sw_thermal_slowdown": nv.nvmlClocksEventReasonSwThermalSlowdown,
                  "sw_power_cap": nv.nvmlClocksEventReasonSwPowerCap,
-                 "hw_power_brake_slowdown": nv.nvmlClocksEventReasonHwPowerBrakeSlowdown}
+                 "hw_power_brake_slowdown": nv.nvmlClocksEventReasonHwPowerBrakeSlowdown,
+                 "applications_clocks_setting": nv.nvmlClocksEventReasonApplicationsClocksSetting,
+                 "sync_boost": nv.nvmlClocksEventReasonSyncBoost,
+                 "gpu_idle": nv.nvmlClocksEventReasonGpuIdle}
         while not self._stop.is_set():
             try:
                 self.samples.append(float(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)))
@@ -109,6 +112,7 @@ class ClockSampler:
         if not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
         return {"sm_mhz": float(np.median(self.samples)), "sm_max_mhz": self.max_mhz,
+                "sm_mhz_min_max": [float(min(self.samples)), float(max(self.samples))],
                 "reasons": sorted(self.reasons), "samples": len(self.samples), "source": "NVML, 5 ms period"}
 
 
