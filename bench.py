@@ -133,14 +133,19 @@ def cpu_baseline(steps: int = 1, warmup: int = 0):
     k = rng.standard_normal((1, 1, S, D), dtype=np.float32)
     v = rng.standard_normal((1, 1, S, D), dtype=np.float32)
     do = rng.standard_normal((1, g, S, D), dtype=np.float32)
-    for _ in range(warmup):
-        cpu_sample_step(q, k, v, do)
-    t0 = time.perf_counter()
-    for _ in range(steps):
-        cpu_sample_step(q, k, v, do)
-    dt = (time.perf_counter() - t0) / steps
+    # All host threads for the BLAS the oracle's numpy matmuls run on (torchrun
+    # sets OMP_NUM_THREADS=1, which would otherwise pin it to one core).
+    from threadpoolctl import threadpool_info, threadpool_limits
+    with threadpool_limits(limits=os.cpu_count() or 1, user_api="blas"):
+        cores = max([i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"] or [1])
+        for _ in range(warmup):
+            cpu_sample_step(q, k, v, do)
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            cpu_sample_step(q, k, v, do)
+        dt = (time.perf_counter() - t0) / steps
     unit_flop = STEP_FLOP / UNITS
-    return {"value": unit_flop / dt / 1e12, "unit": "TFLOP/s", "cores": torch.get_num_threads(),
+    return {"value": unit_flop / dt / 1e12, "unit": "TFLOP/s", "cores": cores,
             "kind": "port",
             "sample": f"1 of {UNITS} (batch, kv-head group) units of config 2 (4 q heads x 4096 x 128, causal), "
                       f"numpy fp32 naive fwd + closed-form VJP, {dt:.2f} s/unit, scaled by unit FLOP"}
