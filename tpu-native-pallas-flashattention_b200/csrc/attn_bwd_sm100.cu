@@ -42,7 +42,12 @@ namespace {
 constexpr int kEWG = PF_BWD_EWG;
 constexpr int kNCH = 4 / kEWG;                // 32-column chunks per elementwise thread
 constexpr int kEWThreads = 128 * kEWG;
-constexpr int kThreads = 64 + kEWThreads;
+// Warp kCertWarp is the data certifier: it adds one arrival to each phase of
+// two elementwise barriers once the tiles the MMA issuer reads after that
+// phase have landed, so the issuer polls only the elementwise barriers (each
+// poll it waits on costs tensor-core time).
+constexpr int kCertWarp = 2 + 4 * kEWG;
+constexpr int kThreads = 64 + kEWThreads + 32;
 
 struct BwdBars {
   uint64_t fixed;                  // the CTA's resident tiles
@@ -273,9 +278,9 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
     mbar_init(&bars->s_full[0], 1);
     mbar_init(&bars->dp_full, 1);
     mbar_init(&bars->p_ready, kEWThreads);
-    mbar_init(&bars->ds_ready, kEWThreads);
+    mbar_init(&bars->ds_ready, kEWThreads + 1);  // + certifier: dO(it+1) landed
     mbar_init(&bars->pv_done, 1);
-    mbar_init(&bars->s_free, kEWThreads);
+    mbar_init(&bars->s_free, kEWThreads + 1);  // + certifier: Q(it+1) and its statistics landed
     mbar_init(&bars->done, 1);
     fence_barrier_init();
   }
@@ -317,6 +322,7 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
         }
       };
       fetch_stats(0);
+      int last_q = -1, last_do = -1;
       for (int it = 0; it < n_it; ++it) {
         const int s = it % NS;
         if (it >= NS && !mbar_wait(&bars->empty[s], ((it / NS) - 1) & 1)) break;
@@ -329,6 +335,7 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
           for (int c = 0; c < Cfg::kBoxes; ++c)
             tma_load_3d(qdst + c * 128 * 128, &tm_q, &bars->full[s], c * 64, qi * 128, plane);
         }
+        last_q = it;
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           stats[s * 256 + lane + 32 * u] = pl[u];
@@ -343,6 +350,12 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
           for (int c = 0; c < Cfg::kBoxes; ++c)
             tma_load_3d(qdst + Cfg::kTile + c * 128 * 128, &tm_do, &bars->vfull[s], c * 64, qi * 128, plane);
         }
+        last_do = it;
+      }
+      if (lane == 0) {  // exit drain: no copy may land after the CTA is gone
+        mbar_wait(&bars->fixed, 0);
+        drain_ring(bars->full, NS, last_q);
+        drain_ring(bars->vfull, NS, last_do);
       }
     }
   } else if (warp == 1) {
@@ -371,7 +384,7 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
         umma_commit(&bars->s_full[0]);
       };
       auto issue_dp = [&](int it) -> bool {
-        if (!mbar_wait_spin(&bars->vfull[it % NS], (it / NS) & 1)) return false;
+        if (it == 0 && !mbar_wait_spin(&bars->vfull[0], 0)) return false;  // later tiles: certified
         tc_fence_after();
         const uint32_t do_addr = stage(it) + Cfg::kTile;
         const uint64_t od = desc_k_base<128>(do_addr);
@@ -395,8 +408,7 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
         bool need_s = it + 1 < n_it, need_v = true;
         const uint64_t t0 = global_timer_ns();
         for (uint32_t spin = 1; ok && (need_s || need_v); ++spin) {
-          if (need_s && mbar_test(&bars->s_free, it & 1) &&
-              mbar_test(&bars->full[(it + 1) % NS], ((it + 1) / NS) & 1)) {
+          if (need_s && mbar_test(&bars->s_free, it & 1)) {  // Q(it+1) certified in the phase
             trace(14, it);
             tc_fence_after();
             issue_s(it + 1);
@@ -434,6 +446,21 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
       }
       umma_commit(&bars->done);
     }
+  } else if (warp == kCertWarp) {
+    if (lane == 0) {
+      bool ok = true;
+      for (int it = 0; ok && it < n_it; ++it) {
+        const bool next = it + 1 < n_it;
+        if (next) ok = mbar_wait(&bars->full[(it + 1) % NS], ((it + 1) / NS) & 1);
+        if (!ok) break;
+        mbar_arrive(&bars->s_free);
+        if (next) ok = mbar_wait(&bars->vfull[(it + 1) % NS], ((it + 1) / NS) & 1);
+        if (!ok) break;
+        mbar_arrive(&bars->ds_ready);
+        // Never arrive twice in one phase.
+        ok = mbar_wait(&bars->s_free, it & 1) && mbar_wait(&bars->ds_ready, it & 1);
+      }
+    }
   } else if (warp >= 2) {
     const int cw = (warp - 2) / 4;      // elementwise warpgroup
     const int col0 = 32 * kNCH * cw;    // its first query column of the tile
@@ -460,8 +487,11 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
       uint32_t keep[kNCH][16], pk[kNCH][16];
       {
         uint32_t rs[kNCH][32];
-#pragma unroll
-        for (int h = 0; h < kNCH; ++h) tmem_ld32(lane_base + Cfg::kS + col0 + 32 * h, rs[h]);
+  if constexpr (kNCH == 2) {
+          tmem_ld64x1(lane_base + Cfg::kS + col0, rs);
+        } else {
+          tmem_ld32(lane_base + Cfg::kS + col0, rs[0]);
+        }
         tmem_wait_ld();
         tc_fence_before();
         mbar_arrive(&bars->s_free);  // S(it+1) may now overwrite the tile
@@ -525,6 +555,9 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
+    // `done` follows every MMA this CTA issued (committed after the issue
+    // loop on every path), so TMEM is never freed under a running MMA.
+    if (lane == 0 && n_it > 0) mbar_wait(&bars->done, 0);
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, 512);
@@ -577,8 +610,8 @@ bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     mbar_init(&bars->s_full[0], 1);
     mbar_init(&bars->s_full[1], 1);
     mbar_init(&bars->dp_full, 1);
-    mbar_init(&bars->dp_free, kEWThreads);
-    mbar_init(&bars->ds_ready, kEWThreads);
+    mbar_init(&bars->dp_free, kEWThreads + 1);   // + certifier: V(it+1) landed
+    mbar_init(&bars->ds_ready, kEWThreads + 1);  // + certifier: K(it+2) landed
     mbar_init(&bars->done, 1);
     fence_barrier_init();
   }
@@ -599,6 +632,7 @@ bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         tma_load_3d(smem + Cfg::kFixedOff + Cfg::kTile + c * 128 * 128, &tm_do, &bars->fixed, c * 64, q0, bh);
       }
       const int kv_plane = b * Hkv + hk;
+      int last_k = -1, last_v = -1;
       for (int it = 0; it < n_it; ++it) {
         const int sk = it % NK, sv = it % NV;
         if (it >= NK && !mbar_wait(&bars->empty[sk], ((it / NK) - 1) & 1)) break;
@@ -606,12 +640,18 @@ bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         for (int c = 0; c < Cfg::kBoxes; ++c)
           tma_load_3d(smem + Cfg::kKOff + sk * Cfg::kTile + c * 128 * 128, &tm_k, &bars->full[sk], c * 64,
                       it * 128, kv_plane);
+        last_k = it;
         if (it >= NV && !mbar_wait(&bars->vempty[sv], ((it / NV) - 1) & 1)) break;
         mbar_expect_tx(&bars->vfull[sv], Cfg::kTile);
         for (int c = 0; c < Cfg::kBoxes; ++c)
           tma_load_3d(smem + Cfg::kVOff + sv * Cfg::kTile + c * 128 * 128, &tm_v, &bars->vfull[sv], c * 64,
                       it * 128, kv_plane);
+        last_v = it;
       }
+      // Exit drain: no copy may land after the CTA is gone.
+      mbar_wait(&bars->fixed, 0);
+      drain_ring(bars->full, NK, last_k);
+      drain_ring(bars->vfull, NV, last_v);
     }
   } else if (warp == 1) {
     // Tensor-core order per iteration:
@@ -626,8 +666,8 @@ bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       const uint32_t q_addr = sbase + Cfg::kFixedOff, do_addr = q_addr + Cfg::kTile;
       const uint64_t qd = desc_k_base<128>(q_addr), od = desc_k_base<128>(do_addr);
       auto k_tile = [&](int it) { return sbase + Cfg::kKOff + (it % NK) * Cfg::kTile; };
-      auto issue_s = [&](int it) -> bool {
-        if (!mbar_wait_spin(&bars->full[it % NK], (it / NK) & 1)) return false;
+      auto issue_s = [&](int it) -> bool {  // K(0), K(1) polled here; later tiles certified
+        if (it < 2 && !mbar_wait_spin(&bars->full[it % NK], (it / NK) & 1)) return false;
         tc_fence_after();
         const uint32_t k_addr = k_tile(it);
         const uint64_t kdesc = desc_k_base<128>(k_addr);
@@ -638,8 +678,8 @@ bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         umma_commit(&bars->s_full[it & 1]);
         return true;
       };
-      auto issue_dp = [&](int it) -> bool {
-        if (!mbar_wait_spin(&bars->vfull[it % NV], (it / NV) & 1)) return false;
+      auto issue_dp = [&](int it) -> bool {  // V(0) polled here; later tiles certified
+        if (it == 0 && !mbar_wait_spin(&bars->vfull[0], 0)) return false;
         tc_fence_after();
         const uint32_t v_addr = sbase + Cfg::kVOff + (it % NV) * Cfg::kTile;
         const uint64_t vdesc = desc_k_base<128>(v_addr);
@@ -676,6 +716,20 @@ bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       }
       umma_commit(&bars->done);
     }
+  } else if (warp == kCertWarp) {
+    if (lane == 0) {
+      bool ok = true;
+      for (int it = 0; ok && it < n_it; ++it) {
+        if (it + 1 < n_it) ok = mbar_wait(&bars->vfull[(it + 1) % NV], ((it + 1) / NV) & 1);
+        if (!ok) break;
+        mbar_arrive(&bars->dp_free);
+        if (it + 2 < n_it) ok = mbar_wait(&bars->full[(it + 2) % NK], ((it + 2) / NK) & 1);
+        if (!ok) break;
+        mbar_arrive(&bars->ds_ready);
+        // Never arrive twice in one phase.
+        ok = mbar_wait(&bars->dp_free, it & 1) && mbar_wait(&bars->ds_ready, it & 1);
+      }
+    }
   } else if (warp >= 2) {
     const int cw = (warp - 2) / 4;      // elementwise warpgroup
     const int col0 = 32 * kNCH * cw;    // its first key column of the tile
@@ -700,8 +754,11 @@ bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       {
         uint32_t rs[kNCH][32];
         uint32_t unused[16];
-#pragma unroll
-        for (int h = 0; h < kNCH; ++h) tmem_ld32(s_addr + 32 * h, rs[h]);
+  if constexpr (kNCH == 2) {
+          tmem_ld64x1(s_addr, rs);
+        } else {
+          tmem_ld32(s_addr, rs[0]);
+        }
         tmem_wait_ld();
 #pragma unroll
         for (int h = 0; h < kNCH; ++h) {
@@ -721,8 +778,11 @@ bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       tc_fence_after();
       {
         uint32_t rd[kNCH][32];
-#pragma unroll
-        for (int h = 0; h < kNCH; ++h) tmem_ld32(lane_base + Cfg::kDP + col0 + 32 * h, rd[h]);
+  if constexpr (kNCH == 2) {
+          tmem_ld64x1(lane_base + Cfg::kDP + col0, rd);
+        } else {
+          tmem_ld32(lane_base + Cfg::kDP + col0, rd[0]);
+        }
         tmem_wait_ld();
         tc_fence_before();
         mbar_arrive(&bars->dp_free);  // dP(it+1) may now overwrite the tile
@@ -732,6 +792,10 @@ bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       }
       tmem_wait_st();
       tc_fence_before();
+      // The certifier's arrival for phase it-1 waits on K(it+1); without this
+      // wait the elementwise warps could complete phase it-1 for it with
+      // their phase-it arrivals (nothing else orders them after it).
+      if (it > 0 && !mbar_wait_spin(&bars->ds_ready, (it - 1) & 1)) { ok = false; break; }
       mbar_arrive(&bars->ds_ready);
       if (tr) trace(10 + 3 * cw, it);
     }
@@ -746,6 +810,9 @@ bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
+    // `done` follows every MMA this CTA issued (committed after the issue
+    // loop on every path), so TMEM is never freed under a running MMA.
+    if (lane == 0 && n_it > 0) mbar_wait(&bars->done, 0);
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, 512);

@@ -36,7 +36,7 @@ namespace {
 
 constexpr int kBM = 128;        // rows per query tile (= TMEM lanes)
 constexpr int kBN = 128;        // keys per kv tile
-constexpr int kThreads = 320;   // 10 warps: 0-7 softmax, 8 TMA, 9 MMA
+constexpr int kThreads = 352;   // 11 warps: 0-7 softmax, 8 TMA, 9 MMA, 10 data certifier
 constexpr float kRescaleThresh = 8.0f;  // log2 units
 
 template <int D>
@@ -62,6 +62,7 @@ struct Bars {
   uint64_t q_ready[2];  // RoPE: query tile w rotated in shared memory
   uint64_t k_full[4], v_full[4], k_empty[4], v_empty[4];
   uint64_t s_full[2], p_full[2], o_done[2];
+  uint64_t drained;     // follows every MMA of the CTA (committed after the issue loop)
   uint32_t tmem_base;
 };
 
@@ -160,9 +161,10 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       mbar_init(&bars->k_empty[s], 1);
       mbar_init(&bars->v_empty[s], 1);
     }
+    mbar_init(&bars->drained, 1);
     for (int w = 0; w < 2; ++w) {
       mbar_init(&bars->s_full[w], 1);
-      mbar_init(&bars->p_full[w], kBM);
+      mbar_init(&bars->p_full[w], kBM + 1);  // softmax threads + the data certifier
       mbar_init(&bars->o_done[w], 1);
     }
     fence_barrier_init();
@@ -192,6 +194,7 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       }
       const int kv_plane = b * Hkv + hk;
       // Issue order K0, K1, V0, K2, V1, ...: K one step ahead of V.
+      int last_k = -1, last_v = -1;
       auto load_k = [&](int j) -> bool {
         const int s = j % KS;
         if (j >= KS && !mbar_wait(&bars->k_empty[s], ((j / KS) - 1) & 1)) return false;
@@ -199,6 +202,7 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         for (int c = 0; c < Cfg::kBoxes; ++c)
           tma_load_3d(smem + Cfg::kKOff + s * Cfg::kTileBytes + c * kBN * 128, &tm_k,
                       &bars->k_full[s], c * 64, j * kBN, kv_plane);
+        last_k = j;
         trace(12, j);
         return true;
       };
@@ -209,6 +213,7 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         for (int c = 0; c < Cfg::kBoxes; ++c)
           tma_load_3d(smem + Cfg::kVOff + s * Cfg::kTileBytes + c * kBN * 128, &tm_v,
                       &bars->v_full[s], c * 64, j * kBN, kv_plane);
+        last_v = j;
         trace(13, j);
         return true;
       };
@@ -217,6 +222,10 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         if (j < n_max) okp = load_k(j);
         okp = okp && load_v(j - 1);
       }
+      // Exit drain: no copy may land after the CTA is gone.
+      if (active > 0) mbar_wait(&bars->q, 0);
+      drain_ring(bars->k_full, KS, last_k);
+      drain_ring(bars->v_full, VS, last_v);
     }
   } else if (warp == 9) {
     // ------------------------------ MMA issuer ----------------------------
@@ -251,15 +260,16 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         for (int kk = 1; kk < kBN / 16; ++kk) umma_ts_acc(dst, src + kk * 8, vd + mnoff(kk), idesc_pv);
         umma_commit(&bars->o_done[w]);
       };
+      // Tile data is certified by warp 10 inside the p_full phases: p_full[w](j)
+      // completes only once V(j) and K(j+1) are in shared memory, so apart
+      // from K(0) this thread polls nothing but the two softmax barriers (each
+      // poll it waits on costs tensor-core time).
+      if (ok) {
+        ok = mbar_wait_spin(&bars->k_full[0], 0);
+        tc_fence_after();
+      }
       for (int j = 0; ok && j <= n_max; ++j) {
         const int ks = j % KS, vs = j % VS;
-        const bool need_k = (j < n_w[0]) || (j < n_w[1]);
-        if (need_k) {
-          ok = mbar_wait_spin(&bars->k_full[ks], (j / KS) & 1);
-          if (!ok) break;
-          trace(1, j);
-          tc_fence_after();
-        }
         if (j < n_w[0]) {
           issue_s(0, j);
           trace(2, j);
@@ -267,7 +277,7 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         }
         if (j >= 1 && j - 1 < n_w[1]) {
           const int vp = (j - 1) % VS;
-          ok = mbar_wait_spin(&bars->p_full[1], (j - 1) & 1) && mbar_wait_spin(&bars->v_full[vp], ((j - 1) / VS) & 1);
+          ok = mbar_wait_spin(&bars->p_full[1], (j - 1) & 1);
           if (!ok) break;
           trace(3, j - 1);
           tc_fence_after();
@@ -280,13 +290,34 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
           umma_commit(&bars->k_empty[ks]);  // last reader of K_j
         }
         if (j < n_w[0]) {
-          ok = mbar_wait_spin(&bars->p_full[0], j & 1) && mbar_wait_spin(&bars->v_full[vs], (j / VS) & 1);
+          ok = mbar_wait_spin(&bars->p_full[0], j & 1);
           if (!ok) break;
           trace(6, j);
           tc_fence_after();
           issue_pv(0, j);
           if (j >= n_w[1]) umma_commit(&bars->v_empty[vs]);
         }
+      }
+      umma_commit(&bars->drained);
+    }
+  } else if (warp == 10) {
+    // --------------------------- data certifier ---------------------------
+    // Adds one arrival to each softmax barrier phase once the tiles the MMA
+    // issuer will read after that phase (V(j) for PV(j), K(j+1) for the next
+    // S MMAs) have landed, then waits for the phase to complete so it never
+    // arrives twice in one phase.
+    if (lane == 0) {
+      bool ok = true;
+      for (int j = 0; ok && j < n_max; ++j) {
+        ok = mbar_wait(&bars->v_full[j % VS], (j / VS) & 1);
+        if (ok && j + 1 < n_max) ok = mbar_wait(&bars->k_full[(j + 1) % KS], ((j + 1) / KS) & 1);
+        if (!ok) break;
+#pragma unroll
+        for (int w = 0; w < 2; ++w)
+          if (j < n_w[w]) mbar_arrive(&bars->p_full[w]);
+#pragma unroll
+        for (int w = 0; w < 2; ++w)
+          if (ok && j < n_w[w]) ok = mbar_wait(&bars->p_full[w], j & 1);
       }
     }
   } else if (warp < 8) {
@@ -434,6 +465,7 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   tc_fence_before();
   __syncthreads();
   if (warp == 9) {
+    if (lane == 0 && n_max > 0) mbar_wait(&bars->drained, 0);  // no MMA may still write TMEM
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, Cfg::kTmemCols);
