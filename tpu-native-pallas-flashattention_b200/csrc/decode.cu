@@ -147,7 +147,8 @@ decode_split_kernel(DecodeArgs a, int head_chunks) {
   }
 
   bool ok_all = true;
-  for (int t = 0; t < n_tiles; ++t) {
+  int t_stop = 0;  // first tile not consumed
+  for (int t = 0; t < n_tiles; ++t, t_stop = t) {
     const int nv = tile_valid(t);
     if (nv <= 0) break;  // later tiles of this warp are empty too
     if (!mbar_wait(&wbar[t % S], (t / S) & 1)) { ok_all = false; break; }
@@ -205,6 +206,12 @@ decode_split_kernel(DecodeArgs a, int head_chunks) {
     if (lane == 0 && t + S < n_tiles) issue(t + S);
     __syncwarp();
   }
+  // Exit drain (only a timed-out wait leaves copies in flight): tiles
+  // [0, t_stop + S) were issued, those before t_stop consumed.
+  if (lane == 0)
+    for (int u = t_stop; u < t_stop + S && u < n_tiles; ++u)
+      if (tile_valid(u) > 0) mbar_wait(&wbar[u % S], (u / S) & 1);
+  __syncwarp();
 
   // Merge the warps' states, then write this split's partial.
   float* myred = sRed + warp * GC * (D + 2);

@@ -178,7 +178,8 @@ decode_tc_kernel(DecodeArgs a, const __grid_constant__ CUtensorMap tm_k, const _
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
   const float sl2 = a.sm_scale * kLog2e;
 
-  for (int t = 0; t < n_tiles; ++t) {
+  int t_stop = 0;  // first tile not consumed
+  for (int t = 0; t < n_tiles; ++t, t_stop = t) {
     const int nv = tile_valid(t);
     if (nv <= 0) break;
     if (!mbar_wait(&wbar[t % kStages], (t / kStages) & 1)) break;
@@ -278,6 +279,12 @@ decode_tc_kernel(DecodeArgs a, const __grid_constant__ CUtensorMap tm_k, const _
     if (lane == 0 && t + kStages < n_tiles) issue(t + kStages);
     __syncwarp();
   }
+  // Exit drain (only a timed-out wait leaves copies in flight): tiles
+  // [0, t_stop + kStages) were issued, those before t_stop consumed.
+  if (lane == 0)
+    for (int u = t_stop; u < t_stop + kStages && u < n_tiles; ++u)
+      if (tile_valid(u) > 0) mbar_wait(&wbar[u % kStages], (u / kStages) & 1);
+  __syncwarp();
   // Row sums across the quad.
   l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
   l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
