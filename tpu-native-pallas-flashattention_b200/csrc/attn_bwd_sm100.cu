@@ -31,23 +31,33 @@ namespace pf {
 namespace {
 
 
-// Warp 0: TMA producer; warp 1: MMA issuer; warps 2 .. 2 + 4*kEWG - 1: kEWG
-// elementwise warpgroups, each owning 128/kEWG columns of a tile (a warp
+// Warp 0: TMA producer; warp 1: MMA issuer; warps 2 .. 2 + 4*EWG - 1: EWG
+// elementwise warpgroups, each owning 128/EWG columns of a tile (a warp
 // reads TMEM lane quadrant warp % 4, so every four consecutive warps cover
-// the 128 lanes).  More elementwise warps hide more of the dependent-latency
-// chains of the P and dS steps; fewer leave more registers per thread.
-#ifndef PF_BWD_EWG
-#define PF_BWD_EWG 2
+// the 128 lanes); warp kCertWarp: the data certifier, which adds one arrival
+// to each phase of two elementwise barriers once the tiles the MMA issuer
+// reads after that phase have landed, so the issuer polls only the
+// elementwise barriers (each poll it waits on costs tensor-core time).
+// More elementwise warps hide more of the dependent-latency chains of the P
+// and dS steps; fewer leave more registers per thread and less issue
+// pressure beside the MMA warp.  Measured best (interleaved A/B, min over
+// rounds): 2 warpgroups for both kernels.
+template <int EWG>
+struct Ew {
+  static constexpr int kEWG = EWG;
+  static constexpr int kNCH = 4 / EWG;  // 32-column chunks per elementwise thread
+  static constexpr int kEWThreads = 128 * EWG;
+  static constexpr int kCertWarp = 2 + 4 * EWG;
+  static constexpr int kThreads = 64 + kEWThreads + 32;
+};
+#ifndef PF_DKV_EWG
+#define PF_DKV_EWG 2
 #endif
-constexpr int kEWG = PF_BWD_EWG;
-constexpr int kNCH = 4 / kEWG;                // 32-column chunks per elementwise thread
-constexpr int kEWThreads = 128 * kEWG;
-// Warp kCertWarp is the data certifier: it adds one arrival to each phase of
-// two elementwise barriers once the tiles the MMA issuer reads after that
-// phase have landed, so the issuer polls only the elementwise barriers (each
-// poll it waits on costs tensor-core time).
-constexpr int kCertWarp = 2 + 4 * kEWG;
-constexpr int kThreads = 64 + kEWThreads + 32;
+#ifndef PF_DQ_EWG
+#define PF_DQ_EWG 2
+#endif
+using EwDkv = Ew<PF_DKV_EWG>;
+using EwDq = Ew<PF_DQ_EWG>;
 
 struct BwdBars {
   uint64_t fixed;                  // the CTA's resident tiles
@@ -171,6 +181,10 @@ __device__ __forceinline__ void ds_chunk(const uint32_t (&rd)[32], const float (
   tmem_st16(out, pk);
 }
 
+// The thread's 32 or 64 consecutive TMEM columns (one instruction either way).
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[1][32]) { tmem_ld32(taddr, r[0]); }
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[2][32]) { tmem_ld64x1(taddr, r); }
+
 // N consecutive floats of a shared-memory array into registers.
 template <int N>
 __device__ __forceinline__ void load_cols(const float* src, float (&dst)[N]) {
@@ -232,7 +246,7 @@ __device__ __forceinline__ void store_acc_row(uint32_t taddr, T* dst, int n, flo
 // dK / dV
 // ============================================================================
 template <typename T, int D>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(EwDkv::kThreads, 1)
 bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                      const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
                      const float* __restrict__ lse, const float* __restrict__ delta,
@@ -240,6 +254,8 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
                      int kv_len, int causal, float sm_scale, float scale_log2, int n_kt) {
   using Cfg = DkvCfg<D>;
   constexpr int NS = Cfg::kNS;
+  constexpr int kEWG = EwDkv::kEWG, kNCH = EwDkv::kNCH, kEWThreads = EwDkv::kEWThreads;
+  constexpr int kCertWarp = EwDkv::kCertWarp;
   constexpr int FMT = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
   constexpr uint32_t idesc_s = make_idesc_f16(FMT, 128, 128, 0, 0);
   constexpr uint32_t idesc_acc = make_idesc_f16(FMT, 128, D, 0, 1);
@@ -487,11 +503,7 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
       uint32_t keep[kNCH][16], pk[kNCH][16];
       {
         uint32_t rs[kNCH][32];
-  if constexpr (kNCH == 2) {
-          tmem_ld64x1(lane_base + Cfg::kS + col0, rs);
-        } else {
-          tmem_ld32(lane_base + Cfg::kS + col0, rs[0]);
-        }
+        tmem_ld_cols(lane_base + Cfg::kS + col0, rs);
         tmem_wait_ld();
         tc_fence_before();
         mbar_arrive(&bars->s_free);  // S(it+1) may now overwrite the tile
@@ -568,7 +580,7 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
 // dQ
 // ============================================================================
 template <typename T, int D>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(EwDq::kThreads, 1)
 bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
                     const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                     const float* __restrict__ lse, const float* __restrict__ delta, T* __restrict__ dq,
@@ -576,6 +588,8 @@ bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                     int n_qt) {
   using Cfg = DqCfg<D>;
   constexpr int NK = Cfg::kNK, NV = Cfg::kNV;
+  constexpr int kNCH = EwDq::kNCH, kEWThreads = EwDq::kEWThreads;
+  constexpr int kCertWarp = EwDq::kCertWarp;
   constexpr int FMT = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
   constexpr uint32_t idesc_s = make_idesc_f16(FMT, 128, 128, 0, 0);
   constexpr uint32_t idesc_acc = make_idesc_f16(FMT, 128, D, 0, 1);
@@ -754,11 +768,7 @@ bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       {
         uint32_t rs[kNCH][32];
         uint32_t unused[16];
-  if constexpr (kNCH == 2) {
-          tmem_ld64x1(s_addr, rs);
-        } else {
-          tmem_ld32(s_addr, rs[0]);
-        }
+        tmem_ld_cols(s_addr, rs);
         tmem_wait_ld();
 #pragma unroll
         for (int h = 0; h < kNCH; ++h) {
@@ -778,11 +788,7 @@ bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       tc_fence_after();
       {
         uint32_t rd[kNCH][32];
-  if constexpr (kNCH == 2) {
-          tmem_ld64x1(lane_base + Cfg::kDP + col0, rd);
-        } else {
-          tmem_ld32(lane_base + Cfg::kDP + col0, rd[0]);
-        }
+        tmem_ld_cols(lane_base + Cfg::kDP + col0, rd);
         tmem_wait_ld();
         tc_fence_before();
         mbar_arrive(&bars->dp_free);  // dP(it+1) may now overwrite the tile
@@ -833,7 +839,7 @@ cudaError_t launch_dkv_t(const BwdArgs& a) {
   cudaError_t e = ensure_smem(kern, Cfg::kSmem);
   if (e != cudaSuccess) return e;
   const int n_kt = (a.Sk + 127) / 128;
-  kern<<<n_kt * BHk, kThreads, Cfg::kSmem, a.stream>>>(tk, tv, tq, tdo, a.lse, a.delta, (T*)a.dk, (T*)a.dv, a.H,
+  kern<<<n_kt * BHk, EwDkv::kThreads, Cfg::kSmem, a.stream>>>(tk, tv, tq, tdo, a.lse, a.delta, (T*)a.dk, (T*)a.dv, a.H,
                                                        a.Hkv, a.Sq, a.Sk, a.kv_len, a.causal, a.sm_scale,
                                                        a.sm_scale * kLog2e, n_kt);
   return cudaGetLastError();
@@ -853,7 +859,7 @@ cudaError_t launch_dq_t(const BwdArgs& a) {
   cudaError_t e = ensure_smem(kern, Cfg::kSmem);
   if (e != cudaSuccess) return e;
   const int n_qt = (a.Sq + 127) / 128;
-  kern<<<n_qt * BH, kThreads, Cfg::kSmem, a.stream>>>(tq, tdo, tk, tv, a.lse, a.delta, (T*)a.dq, a.H, a.Hkv,
+  kern<<<n_qt * BH, EwDq::kThreads, Cfg::kSmem, a.stream>>>(tq, tdo, tk, tv, a.lse, a.delta, (T*)a.dq, a.H, a.Hkv,
                                                       a.Sq, a.kv_len, a.causal, a.sm_scale, a.sm_scale * kLog2e,
                                                       n_qt);
   return cudaGetLastError();
