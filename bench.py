@@ -284,6 +284,56 @@ def rope_prefill_bench(pf, dev, iters=5):
             "flop": flop, "ms": ms, "TFLOP/s": flop / ms / 1e9}
 
 
+def c1_forward_bench(pf, dev, iters=50):
+    """Config 1: fp32 forward [1, 8, 512, 128] causal (latency-dominated; 5.37e8 FLOP), with the
+    oracle's numpy fp32 forward on the same inputs timed beside it on the host."""
+    from oracle import attention_oracle as orc
+
+    shape = (1, 8, 512, 128)
+    g = torch.Generator(device=dev).manual_seed(1)
+    q, k, v = (torch.randn(shape, device=dev, generator=g) for _ in range(3))
+    for _ in range(3):
+        pf.flash_attention(q, k, v, causal=True)
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(iters):
+        pf.flash_attention(q, k, v, causal=True)
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / iters
+    # The same call replayed from a CUDA graph: the device time without the
+    # per-call host work of an eager loop.
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(st)
+    with torch.cuda.stream(side):
+        pf.flash_attention(q, k, v, causal=True)
+    st.wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(10):
+            pf.flash_attention(q, k, v, causal=True)
+    graph.replay()
+    torch.cuda.synchronize()
+    e0.record(st)
+    for _ in range(iters // 10):
+        graph.replay()
+    e1.record(st)
+    torch.cuda.synchronize()
+    graph_ms = e0.elapsed_time(e1) / (10 * (iters // 10))
+    qh, kh, vh = (t.cpu().numpy() for t in (q, k, v))
+    t0 = time.perf_counter()
+    orc.reference_attention(qh, kh, vh, causal=True, dtype=np.float32)
+    cpu_ms = (time.perf_counter() - t0) * 1e3
+    flop = 4.0 * 1 * 8 * 512 * 512 * 128 / 2
+    return {"workload": "config 1: fp32 forward [1,8,512,128] causal", "flop": flop,
+            "api_ms": ms, "graph_ms": graph_ms, "TFLOP/s": flop / graph_ms / 1e9,
+            "timing": "api_ms: eager public-API calls; graph_ms: the same call replayed from a CUDA graph "
+                      "(device time without per-call host work)",
+            "kernel": pf._lib.forward_kernel_kind(torch.float32, 128), "cpu_oracle_ms": cpu_ms}
+
+
 def generation_bench(pf, dev):
     """Config 5: tiny-LLaMA greedy generation tokens/s (generate_cached, then ring streaming)."""
     cfg = pf.ModelConfig(vocab_size=32000, dim=512, n_layers=8, n_heads=8, n_kv_heads=2, head_dim=64,
@@ -513,6 +563,7 @@ def main():
         rp = rope_prefill_bench(pf, dev)
         rp["frac_of_bf16_peak"] = rp["TFLOP/s"] / tf_burst
         line["rope_prefill"] = rp
+        line["c1_forward"] = c1_forward_bench(pf, dev)
         line["generation"] = generation_bench(pf, dev)
         line["cpu_baseline"] = cpu_baseline(steps=1)
     if rank == 0:

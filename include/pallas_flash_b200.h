@@ -26,6 +26,10 @@
  *   pf_paged_write      src/pallas_flash/paged.py:205-223            (write_to_paged_cache)
  *   pf_cache_write      src/pallas_flash/model.py:257-262,446-449    (_cache_write / ring slots)
  *   pf_paged_gather     src/pallas_flash/paged.py:158-159            (the block-table index map)
+ *   pf_rope_paged_write src/pallas_flash/model.py:338-342 + paged.py:205-223 (RoPE of the decode
+ *                       token's q/k fused with the k/v page write)
+ *   pf_rope_apply       src/pallas_flash/fused_rope.py:43-50, model.py:41-67 (apply_rope; and its
+ *                       inverse, for the gradient of the RoPE-fused attention)
  */
 #ifndef PALLAS_FLASH_B200_H_
 #define PALLAS_FLASH_B200_H_
@@ -193,6 +197,32 @@ int pf_cache_write(void* k_cache, void* v_cache, const void* k, const void* v,
 int pf_paged_gather(const void* pages, const int32_t* block_tables, void* out,
                     int dtype, int B, int Hkv, int num_pages, int page_size,
                     int pages_per_seq, int D, void* stream);
+
+/* pf_rope_paged_write: the step before decode attention, for one token per
+ *   sequence: q [B, H, 1, D] is rotated in place and k [B, Hkv, 1, D] rotated,
+ *   both at row rope_positions[b] of the [table_rows, D] cos/sin tables
+ *   (clamped into range), then rotated k and v are written like
+ *   pf_paged_write at slot positions[b] (for a ring cache the slot differs
+ *   from the rotation position).  Rotation in fp32, one rounding.
+ */
+int pf_rope_paged_write(void* q, void* k_pages, void* v_pages, const void* k,
+                        const void* v, const void* cos, const void* sin,
+                        int table_dtype, int table_rows, const int32_t* block_tables,
+                        const int32_t* positions, const int32_t* rope_positions,
+                        int dtype, int B, int H, int Hkv, int num_pages, int page_size,
+                        int pages_per_seq, int D, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Rotary embedding.
+ * pf_rope_apply: out = x*cos + rotate_half(x)*sin over rows x[B, H, S, D]
+ *   (rotate_half([x1, x2]) = [-x2, x1]); row s of the [S, D] cos/sin tables
+ *   (table_dtype) belongs to position s.  inverse != 0 applies the transpose
+ *   (sin negated): the gradient map of the rotation.  fp32 arithmetic; out may
+ *   alias x.  D must be even.
+ * ------------------------------------------------------------------------- */
+int pf_rope_apply(const void* x, const void* cos, const void* sin, int table_dtype,
+                  void* out, int dtype, int B, int H, int S, int D, int inverse,
+                  void* stream);
 
 #ifdef __cplusplus
 }

@@ -125,3 +125,59 @@ def test_c3_shape_sampled():
     for i, r in enumerate(rows):
         ref = orc.reference_attention(qrot[:, :, i:i + 1], krot[:, :, :r + 1], vv[:, :, :r + 1], dtype=np.float32)
         assert np.max(np.abs(to_np(out[:, 5:6, r:r + 1]) - ref)) < 2e-2, r
+
+
+# --------------------------------------------------------------------------
+# Gradient of the RoPE-fused attention (an extension: the reference's
+# flash_attention_rope is forward-only, fused_rope.py:25-27).  The oracle is
+# the closed-form attention VJP on the rotated inputs, mapped back through the
+# transposed rotation: d x = R(-theta) d(Rx) (apply_rope with sin negated).
+def _rope_grad_oracle(q, k, v, do, qc, qs, kc, ks, causal, kv_len=None):
+    qr, kr = orc.apply_rope(q, qc, qs), orc.apply_rope(k, kc, ks)
+    dqr, dkr, dv = orc.attention_vjp(qr, kr, v, do, causal=causal, kv_len=kv_len)
+    return orc.apply_rope(dqr, qc, -qs), orc.apply_rope(dkr, kc, -ks), dv
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("H,Hkv,S,D,causal", [(4, 2, 256, 128, True), (2, 2, 200, 64, False), (4, 1, 384, 128, True)])
+def test_rope_attention_grads_match_oracle(dtype, H, Hkv, S, D, causal):
+    from conftest import rel_err
+    q, k, v = randn((1, H, S, D), 11), randn((1, Hkv, S, D), 12), randn((1, Hkv, S, D), 13)
+    do = randn((1, H, S, D), 14)
+    cos, sin = tables(S, D)
+    tq, tk, tv = (to_dev(x, dtype).requires_grad_() for x in (q, k, v))
+    out = pf.flash_attention_rope(tq, tk, tv, cos, sin, causal=causal)
+    out.backward(to_dev(do, dtype))
+    c, s = cos.cpu().numpy(), sin.cpu().numpy()
+    ref = _rope_grad_oracle(widen(tq), widen(tk), widen(tv), widen(to_dev(do, dtype)), c, s, c, s, causal)
+    tol = 1e-4 if dtype == torch.float32 else 2e-2
+    for got, want in zip((tq.grad, tk.grad, tv.grad), ref):
+        assert got.dtype == dtype
+        assert rel_err(to_np(got), want) < tol
+
+
+def test_rope_attention_grads_cross_lengths_and_kv_len():
+    """Separate query/key tables (queries at positions [Sk - Sq, Sk)) and a kv_len mask."""
+    from conftest import rel_err
+    Sq, Sk, kv_len = 64, 320, 300
+    q, k, v = randn((2, 4, Sq, 128), 21), randn((2, 2, Sk, 128), 22), randn((2, 2, Sk, 128), 23)
+    do = randn((2, 4, Sq, 128), 24)
+    cos, sin = tables(Sk)
+    qc, qs = cos[Sk - Sq:], sin[Sk - Sq:]
+    tq, tk, tv = (to_dev(x).requires_grad_() for x in (q, k, v))
+    out = pf.flash_attention_rope(tq, tk, tv, qc, qs, cos, sin, causal=False, kv_len=kv_len)
+    out.backward(to_dev(do))
+    c, s = cos.cpu().numpy(), sin.cpu().numpy()
+    ref = _rope_grad_oracle(q, k, v, do, c[Sk - Sq:], s[Sk - Sq:], c, s, False, kv_len=kv_len)
+    for got, want in zip((tq.grad, tk.grad, tv.grad), ref):
+        assert rel_err(to_np(got), want) < 1e-4
+
+
+def test_rope_apply_inverse_round_trip():
+    x = to_dev(randn((2, 3, 50, 64), 31))
+    cos, sin = tables(50, 64)
+    y = pf.rope_apply(x, cos, sin)
+    ref = orc.apply_rope(to_np(x), cos.cpu().numpy(), sin.cpu().numpy())
+    assert np.max(np.abs(to_np(y) - ref)) < 1e-5
+    back = pf.rope_apply(y, cos, sin, inverse=True)
+    assert float((back - x).abs().max()) < 1e-5

@@ -219,3 +219,40 @@ def test_sequence_sharding_is_bitwise_identical():
         tl = torch.nn.functional.pad(tl, (0, pps - tl.shape[1]))
         part = pf.paged_flash_attention(ql, kl, vl, tl, lt, max_context_len=cap)
         assert torch.equal(part, full[seqs]), seqs
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("H,Hkv,D,ps", [(8, 2, 64, 16), (4, 4, 128, 8)])
+def test_rope_paged_write_matches_unfused(dtype, H, Hkv, D, ps):
+    """Fused decode prologue == apply_rope on q/k (fp32, one rounding) + the page write."""
+    B, pps, rows = 5, 6, 100
+    num_pages = B * pps + 3
+    rng = np.random.default_rng(7)
+    q = randn((B, H, 1, D), 1)
+    k = randn((B, Hkv, 1, D), 2)
+    v = randn((B, Hkv, 1, D), 3)
+    cos, sin = pf.precompute_rope(rows, D, 10000.0, device="cuda")
+    tables = rng.permutation(num_pages)[: B * pps].reshape(B, pps).astype(np.int32)
+    positions = rng.integers(0, pps * ps, size=B).astype(np.int32)
+    rope_rows = rng.integers(0, rows, size=B).astype(np.int32)
+    kp0 = randn((num_pages, Hkv, ps, D), 4)
+    vp0 = randn((num_pages, Hkv, ps, D), 5)
+    tq = to_dev(q, dtype)
+    kp, vp = to_dev(kp0, dtype), to_dev(vp0, dtype)
+    out = pf.rope_write_to_paged_cache_batch(tq, to_dev(k, dtype), to_dev(v, dtype), kp, vp, cos, sin,
+                                             torch.from_numpy(tables), torch.from_numpy(positions),
+                                             torch.from_numpy(rope_rows))
+    assert out.data_ptr() == tq.data_ptr()  # rotated in place
+    c, s = cos.cpu().numpy(), sin.cpu().numpy()
+    tol = 1e-6 if dtype == torch.float32 else 8e-3
+    qw, kw, vw = widen(to_dev(q, dtype)), widen(to_dev(k, dtype)), widen(to_dev(v, dtype))
+    kp_want, vp_want = widen(to_dev(kp0, dtype)), widen(to_dev(vp0, dtype))
+    for b in range(B):
+        r = rope_rows[b]
+        want_q = orc.apply_rope(qw[b:b + 1], c[r:r + 1], s[r:r + 1])
+        assert np.max(np.abs(to_np(tq[b:b + 1]) - want_q)) <= tol * max(1.0, np.max(np.abs(want_q)))
+        page, off = tables[b, positions[b] // ps], positions[b] % ps
+        kp_want[page, :, off] = orc.apply_rope(kw[b:b + 1], c[r:r + 1], s[r:r + 1])[0, :, 0]
+        vp_want[page, :, off] = vw[b, :, 0]
+    np.testing.assert_allclose(widen(kp), kp_want, rtol=0, atol=tol * 8)
+    assert np.array_equal(widen(vp), vp_want)  # v and every untouched slot byte-exact

@@ -69,7 +69,8 @@ fwd_simt_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __res
   float* sK = sQ + kBQ * LD;        // [kBK][LD]
   float* sV = sK + kBK * LD;        // [kBK][LD]
 
-  const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  // Heaviest (last, under causal) query tiles first: they set the tail.
+  const int qb = gridDim.x - 1 - blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int hk = h / (H / Hkv);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int q0 = qb * kBQ;
@@ -97,30 +98,47 @@ fwd_simt_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __res
     load_tile<T>(sV, LD, vp, k0, kBK, kv_len, D, DMAX, nullptr, nullptr, 0);
     __syncthreads();
     const int kpos = k0 + lane;
+    // Scores of this lane's key for all of the warp's rows at once: the rows
+    // are independent FMA chains (columns past D are zero in shared memory).
+    float s[kRowsPerWarp];
+#pragma unroll
+    for (int r = 0; r < kRowsPerWarp; ++r) s[r] = 0.f;
+    const float* qrow = sQ + warp * kRowsPerWarp * LD;
+#pragma unroll 8
+    for (int d = 0; d < DMAX; ++d) {
+      const float kd = sK[lane * LD + d];
+#pragma unroll
+      for (int r = 0; r < kRowsPerWarp; ++r) s[r] = fmaf(qrow[r * LD + d], kd, s[r]);
+    }
+    float p[kRowsPerWarp];
 #pragma unroll
     for (int r = 0; r < kRowsPerWarp; ++r) {
-      const int qi = warp * kRowsPerWarp + r;
-      const int qpos = q0 + qi;
-      float s = 0.f;
-      for (int d = 0; d < D; ++d) s = fmaf(sQ[qi * LD + d], sK[lane * LD + d], s);
-      s *= sm_scale;
+      const int qpos = q0 + warp * kRowsPerWarp + r;
       const bool ok = (kpos < kv_len) && (!causal || qpos >= kpos);
-      s = ok ? s : -INFINITY;
-      const float mt = warp_max(s);
-      const float mn = fmaxf(m[r], mt);
-      if (mn == -INFINITY) continue;  // nothing visible yet for this row
-      const float p = ok ? expf(s - mn) : 0.f;
+      const float sr = ok ? s[r] * sm_scale : -INFINITY;
+      const float mn = fmaxf(m[r], warp_max(sr));
+      if (mn == -INFINITY) {  // nothing visible yet for this row (warp-uniform)
+        p[r] = 0.f;
+        continue;
+      }
+      p[r] = ok ? expf(sr - mn) : 0.f;
       const float alpha = expf(m[r] - mn);  // exp(-inf) = 0 on the first live block
-      l[r] = l[r] * alpha + warp_sum(p);
+      l[r] = l[r] * alpha + warp_sum(p[r]);
       m[r] = mn;
 #pragma unroll
       for (int i = 0; i < NPL; ++i) acc[r][i] *= alpha;
-      for (int j = 0; j < kBK; ++j) {
-        const float pj = __shfl_sync(0xffffffffu, p, j);
-        if (pj != 0.f) {
+    }
+    // O += P V: each V element is loaded once for all rows.
+#pragma unroll 4
+    for (int j = 0; j < kBK; ++j) {
+      float vj[NPL];
 #pragma unroll
-          for (int i = 0; i < NPL; ++i) acc[r][i] = fmaf(pj, sV[j * LD + lane + 32 * i], acc[r][i]);
-        }
+      for (int i = 0; i < NPL; ++i) vj[i] = sV[j * LD + lane + 32 * i];
+#pragma unroll
+      for (int r = 0; r < kRowsPerWarp; ++r) {
+        const float pj = __shfl_sync(0xffffffffu, p[r], j);
+#pragma unroll
+        for (int i = 0; i < NPL; ++i) acc[r][i] = fmaf(pj, vj[i], acc[r][i]);
       }
     }
   }

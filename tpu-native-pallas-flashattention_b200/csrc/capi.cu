@@ -344,4 +344,33 @@ int pf_paged_gather(const void* pages, const int32_t* block_tables, void* out, i
                      "pf_paged_gather");
 }
 
+int pf_rope_apply(const void* x, const void* cos_t, const void* sin_t, int table_dtype, void* out, int dtype,
+                  int B, int H, int S, int D, int inverse, void* stream) {
+  if (!valid_dtype(dtype) || !valid_dtype(table_dtype) || !x || !cos_t || !sin_t || !out)
+    return fail(PF_ERR_INVALID, "pf_rope_apply: bad argument");
+  if (B <= 0 || H <= 0 || S <= 0 || D <= 0) return fail(PF_ERR_INVALID, "pf_rope_apply: shapes must be positive");
+  if (D % 2 != 0) return fail(PF_ERR_INVALID, "pf_rope_apply: head_dim must be even for RoPE");
+  return cuda_status(launch_rope_apply(x, cos_t, sin_t, table_dtype, out, dtype, (long)B * H * S, S, D,
+                                       inverse != 0, static_cast<cudaStream_t>(stream)),
+                     "pf_rope_apply");
+}
+
+int pf_rope_paged_write(void* q, void* k_pages, void* v_pages, const void* k, const void* v, const void* cos_t,
+                        const void* sin_t, int table_dtype, int table_rows, const int32_t* block_tables,
+                        const int32_t* positions, const int32_t* rope_positions, int dtype, int B, int H, int Hkv,
+                        int num_pages, int page_size, int pages_per_seq, int D, void* stream) {
+  if (!valid_dtype(dtype) || !valid_dtype(table_dtype) || !q || !k_pages || !v_pages || !k || !v || !cos_t ||
+      !sin_t || !block_tables || !positions || !rope_positions)
+    return fail(PF_ERR_INVALID, "pf_rope_paged_write: bad argument");
+  if (B <= 0 || H <= 0 || Hkv <= 0 || num_pages <= 0 || page_size <= 0 || pages_per_seq <= 0 || D <= 0 ||
+      table_rows <= 0)
+    return fail(PF_ERR_INVALID, "pf_rope_paged_write: shapes must be positive");
+  if (D % 2 != 0 || D > 1024) return fail(PF_ERR_INVALID, "pf_rope_paged_write: head_dim must be even and <= 1024");
+  if (H % Hkv != 0) return fail(PF_ERR_INVALID, "pf_rope_paged_write: num_heads must be a multiple of num_kv_heads");
+  return cuda_status(launch_rope_paged_write(q, k_pages, v_pages, k, v, cos_t, sin_t, table_dtype, table_rows,
+                                             block_tables, positions, rope_positions, dtype, B, H, Hkv, num_pages,
+                                             page_size, pages_per_seq, D, static_cast<cudaStream_t>(stream)),
+                     "pf_rope_paged_write");
+}
+
 }  // extern "C"

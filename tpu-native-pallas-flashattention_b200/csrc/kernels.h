@@ -85,6 +85,13 @@ cudaError_t launch_paged_write(void* k_pages, void* v_pages, const void* k, cons
 cudaError_t launch_cache_write(void* k_cache, void* v_cache, const void* k, const void* v,
                                int dtype, int B, int Hkv, int C, int L, int D, int start,
                                cudaStream_t stream);
+cudaError_t launch_rope_apply(const void* x, const void* cos_t, const void* sin_t, int tdtype, void* out, int dtype,
+                              long rows, int S, int D, bool inverse, cudaStream_t st);
+cudaError_t launch_rope_paged_write(void* q, void* k_pages, void* v_pages, const void* k, const void* v,
+                                    const void* cos_t, const void* sin_t, int tdtype, int table_rows,
+                                    const int32_t* block_tables, const int32_t* positions,
+                                    const int32_t* rope_pos, int dtype, int B, int H, int Hkv, int num_pages,
+                                    int page_size, int pages_per_seq, int D, cudaStream_t stream);
 cudaError_t launch_paged_gather(const void* pages, const int32_t* block_tables, void* out,
                                 int dtype, int B, int Hkv, int num_pages, int page_size,
                                 int pages_per_seq, int D, cudaStream_t stream);

@@ -14,13 +14,14 @@ from .flash_attention import (
     flash_attention_decode,
     flash_attention_with_lse,
 )
-from .fused_rope import flash_attention_rope
+from .fused_rope import flash_attention_rope, rope_apply
 from .paged import (
     gather_paged,
     init_paged_cache,
     paged_flash_attention,
     write_to_paged_cache,
     write_to_paged_cache_batch,
+    rope_write_to_paged_cache_batch,
 )
 from .reference import reference_attention
 from .model import (
@@ -49,6 +50,7 @@ __all__ = [
     "flash_attention",
     "flash_attention_decode",
     "flash_attention_rope",
+    "rope_apply",
     "paged_flash_attention",
     "init_paged_cache",
     "write_to_paged_cache",
@@ -75,6 +77,7 @@ __all__ = [
     "flash_attention_with_lse",
     "flash_attention_backward",
     "write_to_paged_cache_batch",
+    "rope_write_to_paged_cache_batch",
     "gather_paged",
 ]
 

@@ -60,6 +60,9 @@ _SIGNATURES = {
     "pf_paged_write": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P]),
     "pf_cache_write": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P]),
     "pf_paged_gather": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P]),
+    "pf_rope_apply": (_I, [_P, _P, _P, _I, _P, _I, _I, _I, _I, _I, _I, _P]),
+    "pf_rope_paged_write": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I,
+                                 _P]),
 }
 
 EXPORTED = tuple(_SIGNATURES)

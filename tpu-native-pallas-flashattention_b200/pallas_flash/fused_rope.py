@@ -7,7 +7,14 @@ rotated Q never reaches HBM) and each key row is rotated exactly once into a
 workspace that the attention kernel streams -- the reference instead rotates
 the K block for every (query head, query block) that reads it.  Separate query and
 key tables cover decode, where the query sits at position ``pos`` and keys
-span ``[0, pos]``.  Forward only, like the reference.
+span ``[0, pos]``.
+
+The reference is forward-only (fused_rope.py:25-27).  Here the function is also
+differentiable in q, k and v: when gradients are needed the forward rotates Q
+and K with ``pf_rope_apply`` and runs the attention forward that saves the
+log-sum-exp; the backward runs the attention backward on the rotated tensors
+and maps dQ and dK back through the transposed rotation (sin negated).  The
+tables are treated as constants (no gradient).
 """
 
 from __future__ import annotations
@@ -18,8 +25,51 @@ from typing import Optional
 import torch
 
 from . import _lib
+from .flash_attention import _bwd, _fwd
 
-__all__ = ["flash_attention_rope"]
+__all__ = ["flash_attention_rope", "rope_apply"]
+
+
+def rope_apply(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, *, inverse: bool = False,
+               out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``x*cos + rotate_half(x)*sin`` over ``[B, H, S, D]`` rows on the GPU (fp32 arithmetic).
+
+    ``inverse=True`` applies the transposed rotation (the gradient map).  Row s
+    of the ``[S, D]`` tables belongs to position s (fused_rope.py:43-50).
+    """
+    _lib.require_cuda(x, cos, sin)
+    B, H, S, D = x.shape
+    if tuple(cos.shape) != (S, D) or tuple(sin.shape) != (S, D):
+        raise ValueError(f"cos/sin must have shape {(S, D)}, got {tuple(cos.shape)}, {tuple(sin.shape)}")
+    x = x.contiguous()
+    cos, sin = cos.contiguous(), sin.to(cos.dtype).contiguous()
+    if out is None:
+        out = torch.empty_like(x)
+    _lib.check(_lib.lib().pf_rope_apply(
+        x.data_ptr(), cos.data_ptr(), sin.data_ptr(), _lib.dtype_code(cos.dtype), out.data_ptr(),
+        _lib.dtype_code(x.dtype), B, H, S, D, int(bool(inverse)), _lib.stream_of(x)))
+    return out
+
+
+class _RopeAttentionFn(torch.autograd.Function):
+    """Differentiable RoPE attention: saves the rotated Q/K, out and lse."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, q_cos, q_sin, k_cos, k_sin, causal, sm_scale, kv_len):
+        qr = rope_apply(q, q_cos, q_sin)
+        kr = rope_apply(k, k_cos, k_sin)
+        out, lse = _fwd(qr, kr, v, causal, sm_scale, kv_len, want_lse=True)
+        ctx.save_for_backward(qr, kr, v, out, lse, q_cos, q_sin, k_cos, k_sin)
+        ctx.causal, ctx.sm_scale, ctx.kv_len = causal, sm_scale, kv_len
+        return out
+
+    @staticmethod
+    def backward(ctx, do):
+        qr, kr, v, out, lse, q_cos, q_sin, k_cos, k_sin = ctx.saved_tensors
+        dqr, dkr, dv = _bwd(qr, kr, v, out, lse, do, ctx.causal, ctx.sm_scale, ctx.kv_len)
+        dq = rope_apply(dqr, q_cos, q_sin, inverse=True, out=dqr)
+        dk = rope_apply(dkr, k_cos, k_sin, inverse=True, out=dkr)
+        return dq, dk, dv, None, None, None, None, None, None, None
 
 
 def flash_attention_rope(
@@ -78,6 +128,10 @@ def flash_attention_rope(
     _lib.require_cuda(q, k, v, q_cos, q_sin, k_cos, k_sin)
     tdt = q_cos.dtype
     tables = [t.to(tdt).contiguous() for t in (q_cos, q_sin, k_cos, k_sin)]
+    if not (q.dtype == k.dtype == v.dtype):
+        raise ValueError(f"q, k, v must share a dtype, got {q.dtype}, {k.dtype}, {v.dtype}")
+    if torch.is_grad_enabled() and (q.requires_grad or k.requires_grad or v.requires_grad):
+        return _RopeAttentionFn.apply(q, k, v, *tables, bool(causal), float(sm_scale), int(kv_len))
     q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
     out = torch.empty_like(q)
     L = _lib.lib()

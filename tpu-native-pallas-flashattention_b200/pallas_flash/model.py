@@ -28,7 +28,7 @@ import torch
 from . import _lib
 from .config import ModelConfig
 from .flash_attention import flash_attention, flash_attention_decode
-from .paged import paged_flash_attention, write_to_paged_cache_batch
+from .paged import paged_flash_attention, rope_write_to_paged_cache_batch
 
 Params = Dict[str, Any]
 Cache = list  # per-layer list of {"k": [b, n_kv, cache_size, d], "v": same}
@@ -241,12 +241,16 @@ def _decode_layers(params: Params, token, cache: Cache, pos: int, slot: int, kv_
     x = params["embed"][token]
     cos, sin = _rope_slice(pos, 1, cfg, x.dtype, x.device)
     batch = x.shape[0]
+    # The fixed (or ring) cache [B, Hkv, C, D] as a page pool of one C-token
+    # page per sequence: RoPE of q/k and the k/v write at `slot` in one launch.
+    table = torch.arange(batch, dtype=torch.int32, device=x.device).reshape(batch, 1)
+    slots = torch.full((batch,), slot, dtype=torch.int32, device=x.device)
+    rows = torch.zeros((batch,), dtype=torch.int32, device=x.device)
     for layer, layer_cache in zip(params["layers"], cache):
         h = rms_norm(x, layer["attn_norm"], cfg.rms_norm_eps)
         q, k, v = project_qkv(layer, h, cfg)
-        q = apply_rope(q, cos, sin)
-        k = apply_rope(k, cos, sin)
-        _cache_write(layer_cache, k, v, slot)
+        q = rope_write_to_paged_cache_batch(q, k, v, layer_cache["k"], layer_cache["v"], cos, sin, table,
+                                            slots, rows)
         attn = flash_attention_decode(q, layer_cache["k"], layer_cache["v"], kv_len,
                                       block_k=cfg.block_k)
         x = x + attn.transpose(1, 2).reshape(batch, 1, cfg.dim) @ layer["wo"]
@@ -272,8 +276,8 @@ class DecodeGraph:
     projections, RoPE, cache write, attention, MLP); at batch 16 the host loop,
     not the GPU, sets the token rate.  Here the position lives on the device:
     the fixed (or ring) cache ``[B, Hkv, C, D]`` is addressed as a page pool of
-    one ``C``-token page per sequence, the cache write goes through the paged
-    write kernel at slot ``pos % C`` and attention through the paged decode
+    one ``C``-token page per sequence, RoPE and the cache write go through one
+    fused kernel (table row ``pos``, slot ``pos % C``) and attention through the paged decode
     kernel with device lengths ``min(pos + 1, C)``, so one captured graph
     serves every position.  Kernels, split schedule and RoPE tables are those
     of ``decode_step`` / ``ring_decode_step``.
@@ -287,6 +291,7 @@ class DecodeGraph:
         self.table = torch.arange(batch, dtype=torch.int32, device=device).reshape(batch, 1)
         self.slots = torch.zeros((batch,), dtype=torch.int32, device=device)
         self.lens = torch.zeros((batch,), dtype=torch.int32, device=device)
+        self.rope_rows = torch.zeros((batch,), dtype=torch.int32, device=device)
         self.dtype, self.device = dtype, device
         self.graph = None
 
@@ -298,16 +303,14 @@ class DecodeGraph:
         cfg, p = self.cfg, self.params
         self.slots.copy_((self.pos % self.C).to(torch.int32).expand_as(self.slots))
         self.lens.copy_(torch.clamp(self.pos + 1, max=self.C).to(torch.int32).expand_as(self.lens))
+        self.rope_rows.copy_(self.pos.to(torch.int32).expand_as(self.rope_rows))
         x = p["embed"][self.token]
-        cos = self.cos.index_select(0, self.pos)
-        sin = self.sin.index_select(0, self.pos)
         batch = x.shape[0]
         for layer, lc in zip(p["layers"], self.cache):
             h = rms_norm(x, layer["attn_norm"], cfg.rms_norm_eps)
             q, k, v = project_qkv(layer, h, cfg)
-            q = apply_rope(q, cos, sin)
-            k = apply_rope(k, cos, sin)
-            write_to_paged_cache_batch(lc["k"], lc["v"], k, v, self.table, self.slots)
+            q = rope_write_to_paged_cache_batch(q, k, v, lc["k"], lc["v"], self.cos, self.sin, self.table,
+                                                self.slots, self.rope_rows)
             attn = paged_flash_attention(q, lc["k"], lc["v"], self.table, self.lens, max_context_len=self.C)
             x = x + attn.transpose(1, 2).reshape(batch, 1, cfg.dim) @ layer["wo"]
             h = rms_norm(x, layer["ffn_norm"], cfg.rms_norm_eps)

@@ -23,7 +23,7 @@ import torch
 from . import _lib
 
 __all__ = ["paged_flash_attention", "init_paged_cache", "write_to_paged_cache",
-           "write_to_paged_cache_batch", "gather_paged"]
+           "write_to_paged_cache_batch", "rope_write_to_paged_cache_batch", "gather_paged"]
 
 
 def paged_flash_attention(
@@ -123,6 +123,44 @@ def write_to_paged_cache_batch(k_pages, v_pages, k, v, block_tables, positions):
         pos.data_ptr(), _lib.dtype_code(k_pages.dtype), batch, n_kv, num_pages, page_size,
         tables.shape[1], head_dim, _lib.stream_of(k_pages)))
     return k_pages, v_pages
+
+
+def rope_write_to_paged_cache_batch(q, k, v, k_pages, v_pages, cos, sin, block_tables, positions,
+                                    rope_positions):
+    """The step before decode attention in one launch: RoPE on the token's q and k, then the k/v page write.
+
+    ``q``: ``[batch, num_heads, 1, head_dim]``, rotated in place (and returned);
+    ``k``/``v``: ``[batch, num_kv_heads, 1, head_dim]``; ``cos``/``sin``:
+    ``[rows, head_dim]`` tables, row ``rope_positions[b]`` (clamped into range)
+    rotating sequence b; rotated k and v land like
+    ``write_to_paged_cache_batch`` at slot ``positions[b]``.  Equivalent to
+    ``apply_rope`` on q and k (model.py:338-342) followed by the page write
+    (paged.py:205-223), with the rotation in fp32 and one rounding.
+    """
+    _lib.require_cuda(q, k, v, k_pages, v_pages, cos, sin)
+    batch, n_heads, one, head_dim = q.shape
+    num_pages, n_kv, page_size, _ = k_pages.shape
+    if one != 1 or k.shape != (batch, n_kv, 1, head_dim) or v.shape != k.shape:
+        raise ValueError("q must be [batch, heads, 1, D] and k/v [batch, num_kv_heads, 1, D] of the pools")
+    if tuple(cos.shape) != tuple(sin.shape) or cos.shape[1] != head_dim:
+        raise ValueError(f"cos/sin must be [rows, {head_dim}]")
+    if not (k_pages.is_contiguous() and v_pages.is_contiguous()):
+        raise ValueError("page pools must be contiguous to be written in place")
+    dev = k_pages.device
+    tables = torch.as_tensor(block_tables, dtype=torch.int32, device=dev).reshape(batch, -1).contiguous()
+    pos = torch.as_tensor(positions, dtype=torch.int32, device=dev).reshape(batch).contiguous()
+    rpos = torch.as_tensor(rope_positions, dtype=torch.int32, device=dev).reshape(batch).contiguous()
+    if q.dtype != k_pages.dtype or not q.is_contiguous():
+        q = q.to(k_pages.dtype).contiguous()
+    kk = k.to(k_pages.dtype).contiguous()
+    vv = v.to(v_pages.dtype).contiguous()
+    sin = sin.to(cos.dtype)
+    _lib.check(_lib.lib().pf_rope_paged_write(
+        q.data_ptr(), k_pages.data_ptr(), v_pages.data_ptr(), kk.data_ptr(), vv.data_ptr(),
+        cos.contiguous().data_ptr(), sin.contiguous().data_ptr(), _lib.dtype_code(cos.dtype), cos.shape[0],
+        tables.data_ptr(), pos.data_ptr(), rpos.data_ptr(), _lib.dtype_code(q.dtype), batch, n_heads, n_kv,
+        num_pages, page_size, tables.shape[1], head_dim, _lib.stream_of(q)))
+    return q
 
 
 def write_to_paged_cache(k_pages, v_pages, k, v, block_table, position: int):
