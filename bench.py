@@ -334,6 +334,39 @@ def c1_forward_bench(pf, dev, iters=50):
             "kernel": pf._lib.forward_kernel_kind(torch.float32, 128), "cpu_oracle_ms": cpu_ms}
 
 
+def paged_prefill_bench(pf, dev, iters=5):
+    """Chunked prefill over a page pool: 16 sequences, contexts U[2048, 8192] (seed 0), 512-query
+    chunks at the end of each context, H32/Hkv8/D128 bf16, page 16.  FLOP = 4*H*D * visible keys
+    summed over the chunk rows (causal within the chunk)."""
+    n, L, h, hkv, d, ps = 16, 512, 32, 8, 128, 16
+    rng = np.random.default_rng(0)
+    lens = rng.integers(2048, 8193, size=n)
+    pps = int((lens.max() + ps - 1) // ps)
+    num_pages = n * pps
+    tables = torch.from_numpy(rng.permutation(num_pages).reshape(n, pps).astype(np.int32))
+    g = torch.Generator(device=dev).manual_seed(3)
+    q = torch.randn((n, h, L, d), device=dev, generator=g).to(torch.bfloat16)
+    kp = torch.randn((num_pages, hkv, ps, d), device=dev, generator=g).to(torch.bfloat16)
+    vp = torch.randn((num_pages, hkv, ps, d), device=dev, generator=g).to(torch.bfloat16)
+    ctx = torch.from_numpy(lens.astype(np.int32))
+    mx = int(lens.max())
+    for _ in range(2):
+        pf.paged_prefill_attention(q, kp, vp, tables, ctx, max_context_len=mx)
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(iters):
+        pf.paged_prefill_attention(q, kp, vp, tables, ctx, max_context_len=mx)
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / iters
+    flop = float(sum(4.0 * h * d * (L * (c - L) + L * (L + 1) / 2) for c in lens.tolist()))
+    return {"workload": "paged chunked prefill: 16 seqs, ctx U[2048,8192], chunk 512, H32/Hkv8/D128 bf16, page 16",
+            "flop": flop, "ms": ms, "TFLOP/s": flop / ms / 1e9,
+            "note": "includes the context gather into contiguous rows (one pass over the live pages)"}
+
+
 def generation_bench(pf, dev):
     """Config 5: tiny-LLaMA greedy generation tokens/s (generate_cached, then ring streaming)."""
     cfg = pf.ModelConfig(vocab_size=32000, dim=512, n_layers=8, n_heads=8, n_kv_heads=2, head_dim=64,
@@ -564,6 +597,7 @@ def main():
         rp["frac_of_bf16_peak"] = rp["TFLOP/s"] / tf_burst
         line["rope_prefill"] = rp
         line["c1_forward"] = c1_forward_bench(pf, dev)
+        line["paged_prefill"] = paged_prefill_bench(pf, dev)
         line["generation"] = generation_bench(pf, dev)
         line["cpu_baseline"] = cpu_baseline(steps=1)
     if rank == 0:

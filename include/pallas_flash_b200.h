@@ -28,6 +28,8 @@
  *   pf_paged_gather     src/pallas_flash/paged.py:158-159            (the block-table index map)
  *   pf_rope_paged_write src/pallas_flash/model.py:338-342 + paged.py:205-223 (RoPE of the decode
  *                       token's q/k fused with the k/v page write)
+ *   pf_paged_prefill    extension of src/pallas_flash/paged.py:102-192 to an L-query chunk
+ *                       (the reference pages single-query decode only)
  *   pf_rope_apply       src/pallas_flash/fused_rope.py:43-50, model.py:41-67 (apply_rope; and its
  *                       inverse, for the gradient of the RoPE-fused attention)
  */
@@ -197,6 +199,23 @@ int pf_cache_write(void* k_cache, void* v_cache, const void* k, const void* v,
 int pf_paged_gather(const void* pages, const int32_t* block_tables, void* out,
                     int dtype, int B, int Hkv, int num_pages, int page_size,
                     int pages_per_seq, int D, void* stream);
+
+/* pf_paged_prefill: chunked prefill over a page pool.  q [B, H, L, D] holds the
+ *   last L positions of every sequence (query row i of sequence b sits at
+ *   position context_lens[b] - L + i; its k/v are already in the pages) and
+ *   attends causally to keys [0, position] of its own context, read through
+ *   block_tables as in pf_paged_decode; out like q.  The contexts are first
+ *   gathered into the workspace (pf_paged_prefill_workspace_size bytes,
+ *   16-byte aligned; max_context_len bounds context_lens), then the prefill
+ *   kernels run with per-sequence lengths and causal offsets.  Requires
+ *   D * element size to be a multiple of 16 bytes.
+ */
+size_t pf_paged_prefill_workspace_size(int dtype, int B, int Hkv, int max_context_len, int D);
+int pf_paged_prefill(const void* q, const void* k_pages, const void* v_pages,
+                     const int32_t* block_tables, const int32_t* context_lens, void* out,
+                     int dtype, int B, int H, int Hkv, int L, int num_pages, int page_size,
+                     int pages_per_seq, int D, int max_context_len, float sm_scale,
+                     void* workspace, size_t workspace_bytes, void* stream);
 
 /* pf_rope_paged_write: the step before decode attention, for one token per
  *   sequence: q [B, H, 1, D] is rotated in place and k [B, Hkv, 1, D] rotated,

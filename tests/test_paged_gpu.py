@@ -256,3 +256,60 @@ def test_rope_paged_write_matches_unfused(dtype, H, Hkv, D, ps):
         vp_want[page, :, off] = vw[b, :, 0]
     np.testing.assert_allclose(widen(kp), kp_want, rtol=0, atol=tol * 8)
     assert np.array_equal(widen(vp), vp_want)  # v and every untouched slot byte-exact
+
+
+# --------------------------------------------------------------------------
+# Paged (chunked) prefill -- an extension: the reference pages single-query
+# decode only.  Oracle: the chunk's L queries are the last rows of a causal
+# attention over the gathered context, i.e. reference_attention of a
+# full-length query whose last L rows are the chunk, restricted to those rows.
+def _prefill_oracle(q, k_pages, v_pages, tables, lens):
+    B, H, L, D = q.shape
+    pps = tables.shape[1]
+    out = np.zeros(q.shape)
+    for b, ctx in enumerate(lens):
+        kc = orc.gather_contiguous(k_pages, tables[b], pps, ctx)[None]
+        vc = orc.gather_contiguous(v_pages, tables[b], pps, ctx)[None]
+        q_full = np.zeros((1, H, ctx, D))
+        q_full[:, :, ctx - L:] = q[b:b + 1]
+        out[b] = orc.reference_attention(q_full, kc, vc, causal=True, dtype=np.float64)[0, :, ctx - L:]
+    return out
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("H,Hkv,D,ps,lens,L", [
+    (4, 2, 128, 16, [300, 130, 77], 64),
+    (8, 2, 64, 32, [40, 512], 40),
+    (4, 4, 128, 16, [1000, 129], 129),
+    (2, 1, 128, 8, [257], 256),
+])
+def test_paged_prefill_matches_oracle(dtype, H, Hkv, D, ps, lens, L):
+    B = len(lens)
+    pps = max((n + ps - 1) // ps for n in lens) + 1
+    num_pages = B * pps + 5
+    tables = scrambled_table(B, pps, num_pages, seed=3)
+    q = randn((B, H, L, D), 41)
+    k_pages = randn((num_pages, Hkv, ps, D), 42)
+    v_pages = randn((num_pages, Hkv, ps, D), 43)
+    tq, tk, tv = to_dev(q, dtype), to_dev(k_pages, dtype), to_dev(v_pages, dtype)
+    got = pf.paged_prefill_attention(tq, tk, tv, torch.from_numpy(tables), torch.tensor(lens, dtype=torch.int32))
+    assert got.shape == q.shape and got.dtype == dtype
+    want = _prefill_oracle(widen(tq), widen(tk), widen(tv), tables, lens)
+    tol = 2e-3 if dtype == torch.float32 else 2e-2
+    assert np.max(np.abs(to_np(got) - want)) < tol
+
+
+def test_paged_prefill_single_token_equals_paged_decode():
+    """L = 1 is the decode case: same math as paged_flash_attention (different kernels)."""
+    B, H, Hkv, D, ps = 3, 8, 2, 128, 16
+    lens = [100, 17, 260]
+    pps = 20
+    num_pages = B * pps + 1
+    tables = torch.from_numpy(scrambled_table(B, pps, num_pages, seed=5))
+    q = to_dev(randn((B, H, 1, D), 51), torch.bfloat16)
+    kp = to_dev(randn((num_pages, Hkv, ps, D), 52), torch.bfloat16)
+    vp = to_dev(randn((num_pages, Hkv, ps, D), 53), torch.bfloat16)
+    ctx = torch.tensor(lens, dtype=torch.int32)
+    a = pf.paged_prefill_attention(q, kp, vp, tables, ctx)
+    b = pf.paged_flash_attention(q, kp, vp, tables, ctx)
+    assert float((a.float() - b.float()).abs().max()) < 2e-2

@@ -115,8 +115,9 @@ template <typename T, int D, bool ROPE>
 __global__ void __launch_bounds__(kThreads, 1)
 fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                  const __grid_constant__ CUtensorMap tm_v, T* __restrict__ out,
-                 float* __restrict__ lse, int B, int H, int Hkv, int Sq, int kv_len, int causal,
-                 float scale_log2, int n_qtiles, const void* q_cos, const void* q_sin, int tbl_dtype) {
+                 float* __restrict__ lse, int B, int H, int Hkv, int Sq, int kv_len_max, int causal,
+                 float scale_log2, int n_qtiles, const void* q_cos, const void* q_sin, int tbl_dtype,
+                 const int32_t* __restrict__ kv_lens, const int32_t* __restrict__ q_offs) {
   using Cfg = FwdCfg<D>;
   constexpr int KS = Cfg::kKStages, VS = Cfg::kVStages;
   constexpr int fmt = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
@@ -137,6 +138,9 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   const int b = bh / H, h = bh % H;
   const int hk = h / (H / Hkv);
   const int q_start = qt * 2 * kBM;
+  // Keys of this sequence and the position of query row 0 (causal offset).
+  const int kv_len = kv_lens ? max(0, min(kv_lens[b], kv_len_max)) : kv_len_max;
+  const int q_off = q_offs ? q_offs[b] : 0;
   const int kvb = (kv_len + kBN - 1) / kBN;
   int n_w[2];
 #pragma unroll
@@ -145,8 +149,8 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     if (t0 >= Sq) {
       n_w[w] = 0;
     } else {
-      const int last = min(t0 + kBM - 1, Sq - 1);
-      n_w[w] = causal ? min(kvb, last / kBN + 1) : kvb;
+      const int last = min(t0 + kBM - 1, Sq - 1) + q_off;  // position of the tile's last query
+      n_w[w] = causal ? (last < 0 ? 0 : min(kvb, last / kBN + 1)) : kvb;
     }
   }
   const int n_max = max(n_w[0], n_w[1]);
@@ -345,13 +349,13 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       if (threadIdx.x == 0 || threadIdx.x == 128) trace(8 + 2 * w, j);
       tc_fence_after();
       const int k0 = j * kBN;
-      const bool edge = (k0 + kBN > kv_len) || (causal && k0 + kBN - 1 > q_start + w * kBM);
+      const bool edge = (k0 + kBN > kv_len) || (causal && k0 + kBN - 1 > q_start + w * kBM + q_off);
       // Visible-key count of this row in the tile: keys [k0, k0 + vis) survive
       // both the kv_len and the causal mask.
       int vis = kBN;
       if (edge) {
         vis = min(kBN, kv_len - k0);
-        if (causal) vis = min(vis, qpos - k0 + 1);
+        if (causal) vis = min(vis, qpos + q_off - k0 + 1);
         vis = max(vis, 0);
       }
       // Pass 1: row max.  All four 32-column loads are in flight before the
@@ -488,7 +492,7 @@ cudaError_t launch_t(const FwdArgs& a, const void* k_rot) {
   const float scale_log2 = a.sm_scale * kLog2e;
   kern<<<grid, kThreads, Cfg::kSmem, a.stream>>>(tq, tk, tv, (T*)a.o, a.lse, a.B, a.H, a.Hkv, a.Sq,
                                                  a.kv_len, a.causal, scale_log2, n_qtiles, a.q_cos, a.q_sin,
-                                                 a.tbl_dtype);
+                                                 a.tbl_dtype, a.kv_lens, a.q_offs);
   return cudaGetLastError();
 }
 

@@ -60,8 +60,9 @@ template <typename T, int DMAX>
 __global__ void __launch_bounds__(kThreads)
 fwd_simt_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
                 T* __restrict__ o, float* __restrict__ lse, int H, int Hkv, int Sq, int Sk,
-                int D, int causal, float sm_scale, int kv_len, const void* q_cos,
-                const void* q_sin, const void* k_cos, const void* k_sin, int tbl_dtype) {
+                int D, int causal, float sm_scale, int kv_len_max, const void* q_cos,
+                const void* q_sin, const void* k_cos, const void* k_sin, int tbl_dtype,
+                const int32_t* __restrict__ kv_lens, const int32_t* __restrict__ q_offs) {
   constexpr int LD = DMAX + 1;
   constexpr int NPL = DMAX / 32;  // output dims per lane
   extern __shared__ float smem[];
@@ -74,6 +75,9 @@ fwd_simt_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __res
   const int hk = h / (H / Hkv);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int q0 = qb * kBQ;
+  // Keys of this sequence and the position of query row 0 (causal offset).
+  const int kv_len = kv_lens ? max(0, min(kv_lens[b], kv_len_max)) : kv_len_max;
+  const int q_off = q_offs ? q_offs[b] : 0;
   const T* qp = q + ((long)b * H + h) * Sq * D;
   const T* kp = k + ((long)b * Hkv + hk) * Sk * D;
   const T* vp = v + ((long)b * Hkv + hk) * Sk * D;
@@ -91,7 +95,7 @@ fwd_simt_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __res
 
   // Last key any row of this tile may see (block skipping, :136-147).
   int k_end = kv_len;
-  if (causal) k_end = min(k_end, q0 + kBQ);
+  if (causal) k_end = min(k_end, q0 + q_off + kBQ);
   for (int k0 = 0; k0 < k_end; k0 += kBK) {
     __syncthreads();
     load_tile<T>(sK, LD, kp, k0, kBK, kv_len, D, DMAX, k_cos, k_sin, tbl_dtype);
@@ -114,7 +118,7 @@ fwd_simt_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __res
 #pragma unroll
     for (int r = 0; r < kRowsPerWarp; ++r) {
       const int qpos = q0 + warp * kRowsPerWarp + r;
-      const bool ok = (kpos < kv_len) && (!causal || qpos >= kpos);
+      const bool ok = (kpos < kv_len) && (!causal || qpos + q_off >= kpos);
       const float sr = ok ? s[r] * sm_scale : -INFINITY;
       const float mn = fmaxf(m[r], warp_max(sr));
       if (mn == -INFINITY) {  // nothing visible yet for this row (warp-uniform)
@@ -355,7 +359,7 @@ cudaError_t launch_fwd_t(const FwdArgs& a) {
   dim3 grid((a.Sq + kBQ - 1) / kBQ, a.H, a.B);
   kern<<<grid, kThreads, smem, a.stream>>>(
       (const T*)a.q, (const T*)a.k, (const T*)a.v, (T*)a.o, a.lse, a.H, a.Hkv, a.Sq, a.Sk, a.D,
-      a.causal, a.sm_scale, a.kv_len, a.q_cos, a.q_sin, a.k_cos, a.k_sin, a.tbl_dtype);
+      a.causal, a.sm_scale, a.kv_len, a.q_cos, a.q_sin, a.k_cos, a.k_sin, a.tbl_dtype, a.kv_lens, a.q_offs);
   return cudaGetLastError();
 }
 

@@ -33,6 +33,7 @@ int cuda_status(cudaError_t e, const char* what) {
 }
 
 bool valid_dtype(int d) { return d == PF_F32 || d == PF_BF16 || d == PF_F16; }
+size_t elem_bytes(int d) { return d == PF_F32 ? 4 : 2; }
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 int check_attn_shapes(const char* fn, const void* q, const void* k, const void* v, int dtype,
@@ -371,6 +372,49 @@ int pf_rope_paged_write(void* q, void* k_pages, void* v_pages, const void* k, co
                                              block_tables, positions, rope_positions, dtype, B, H, Hkv, num_pages,
                                              page_size, pages_per_seq, D, static_cast<cudaStream_t>(stream)),
                      "pf_rope_paged_write");
+}
+
+size_t pf_paged_prefill_workspace_size(int dtype, int B, int Hkv, int max_context_len, int D) {
+  if (!valid_dtype(dtype) || B <= 0 || Hkv <= 0 || max_context_len <= 0 || D <= 0) return 0;
+  const size_t plane = (size_t)B * Hkv * max_context_len * D * elem_bytes(dtype);
+  const size_t aligned = (plane + 255) & ~(size_t)255;
+  return 2 * aligned + (size_t)B * sizeof(int32_t);
+}
+
+int pf_paged_prefill(const void* q, const void* k_pages, const void* v_pages, const int32_t* block_tables,
+                     const int32_t* context_lens, void* o, int dtype, int B, int H, int Hkv, int L, int num_pages,
+                     int page_size, int pages_per_seq, int D, int max_context_len, float sm_scale,
+                     void* workspace, size_t workspace_bytes, void* stream) {
+  if (!valid_dtype(dtype) || !q || !k_pages || !v_pages || !block_tables || !context_lens || !o)
+    return fail(PF_ERR_INVALID, "pf_paged_prefill: bad argument");
+  if (B <= 0 || H <= 0 || Hkv <= 0 || L <= 0 || num_pages <= 0 || page_size <= 0 || pages_per_seq <= 0 || D <= 0 ||
+      max_context_len <= 0)
+    return fail(PF_ERR_INVALID, "pf_paged_prefill: shapes must be positive");
+  if (H % Hkv != 0) return fail(PF_ERR_INVALID, "pf_paged_prefill: num_heads must be a multiple of num_kv_heads");
+  const int row_bytes = D * (int)elem_bytes(dtype);
+  if (row_bytes % 16 != 0)
+    return fail(PF_ERR_UNSUPPORTED, "pf_paged_prefill: head_dim * element size must be a multiple of 16 bytes");
+  const int T = max_context_len < pages_per_seq * page_size ? max_context_len : pages_per_seq * page_size;
+  const size_t need = pf_paged_prefill_workspace_size(dtype, B, Hkv, T, D);
+  if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))
+    return fail(PF_ERR_WORKSPACE, "pf_paged_prefill: workspace of %zu bytes required, got %zu", need,
+                workspace_bytes);
+  const size_t plane = (((size_t)B * Hkv * T * row_bytes) + 255) & ~(size_t)255;
+  char* ws = static_cast<char*>(workspace);
+  int32_t* q_offs = reinterpret_cast<int32_t*>(ws + 2 * plane);
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = launch_paged_ctx_gather(k_pages, v_pages, block_tables, context_lens, ws, ws + plane, q_offs, L, B,
+                                          Hkv, num_pages, page_size, pages_per_seq, T, row_bytes, st);
+  if (e != cudaSuccess) return cuda_status(e, "pf_paged_prefill (gather)");
+  FwdArgs a{};
+  a.q = q; a.k = ws; a.v = ws + plane; a.o = o; a.lse = nullptr;
+  a.dtype = dtype; a.B = B; a.H = H; a.Hkv = Hkv; a.Sq = L; a.Sk = T; a.D = D;
+  a.causal = 1; a.kv_len = T; a.sm_scale = sm_scale;
+  a.stream = st;
+  a.kv_lens = context_lens; a.q_offs = q_offs;
+  if (fwd_sm100_supported(dtype, D) && aligned16(q) && aligned16(o))
+    return cuda_status(launch_fwd_sm100(a), "pf_paged_prefill (tcgen05)");
+  return cuda_status(launch_fwd_simt(a), "pf_paged_prefill (simt)");
 }
 
 }  // extern "C"

@@ -372,6 +372,40 @@ __global__ void rope_paged_write_kernel(T* q, T* kp, T* vp, const T* k, const T*
   vp[dst + i + half] = v[src + i + half];
 }
 
+// Paged prefill, step 1: the context of every sequence as contiguous rows
+// [B, Hkv, T, D] (T = the longest context), rows at or past context_lens[b]
+// zero (the attention masks them, and zeros keep 0 * V finite), plus the
+// causal offsets q_offs[b] = context_lens[b] - L of the L-query chunk.
+// 16-byte words; an out-of-range page is flagged and read as page 0.
+__global__ void paged_ctx_gather_kernel(const uint4* __restrict__ kpages, const uint4* __restrict__ vpages,
+                                        const int32_t* __restrict__ tables, const int32_t* __restrict__ ctx,
+                                        uint4* __restrict__ kout, uint4* __restrict__ vout, int32_t* q_offs,
+                                        int L, int B, int Hkv, int num_pages, int ps, int pps, int T, int vec) {
+  if (blockIdx.x == 0)
+    for (int b = threadIdx.x; b < B; b += blockDim.x) q_offs[b] = ctx[b] - L;
+  const long total = (long)B * Hkv * T * vec;
+  for (long idx = blockIdx.x * (long)blockDim.x + threadIdx.x; idx < total; idx += (long)gridDim.x * blockDim.x) {
+    const int c = (int)(idx % vec);
+    const long rowi = idx / vec;          // over (b, hk, t)
+    const int t = (int)(rowi % T);
+    const long plane = rowi / T;          // b * Hkv + hk
+    const int b = (int)(plane / Hkv), hk = (int)(plane % Hkv);
+    uint4 kw = make_uint4(0, 0, 0, 0), vw = kw;
+    if (t < ctx[b] && t < pps * ps) {
+      int page = tables[(long)b * pps + t / ps];
+      if (page < 0 || page >= num_pages) {
+        flag_status(PF_DEV_BAD_PAGE);
+        page = 0;
+      }
+      const long src = (((long)page * Hkv + hk) * ps + t % ps) * vec + c;
+      kw = kpages[src];
+      vw = vpages[src];
+    }
+    kout[idx] = kw;
+    vout[idx] = vw;
+  }
+}
+
 // L tokens into slots (start + i) % C  (model.py:257-262 fixed cache,
 // model.py:434-449 / :475-487 ring buffer).
 template <typename T>
@@ -457,6 +491,20 @@ cudaError_t launch_paged_write(void* k_pages, void* v_pages, const void* k, cons
   else if (dtype == PF_BF16) PF_PW(__nv_bfloat16);
   else PF_PW(__half);
 #undef PF_PW
+  return cudaGetLastError();
+}
+
+cudaError_t launch_paged_ctx_gather(const void* k_pages, const void* v_pages, const int32_t* block_tables,
+                                    const int32_t* context_lens, void* kout, void* vout, int32_t* q_offs, int L,
+                                    int B, int Hkv, int num_pages, int page_size, int pages_per_seq, int T,
+                                    int row_bytes, cudaStream_t stream) {
+  const int vec = row_bytes / 16;
+  const long total = (long)B * Hkv * T * vec;
+  const long want = (total + 255) / 256;
+  const int blocks = (int)(want < 148L * 32 ? (want > 0 ? want : 1) : 148L * 32);
+  paged_ctx_gather_kernel<<<blocks, 256, 0, stream>>>((const uint4*)k_pages, (const uint4*)v_pages, block_tables,
+                                                      context_lens, (uint4*)kout, (uint4*)vout, q_offs, L, B, Hkv,
+                                                      num_pages, page_size, pages_per_seq, T, vec);
   return cudaGetLastError();
 }
 

@@ -18,6 +18,13 @@ struct FwdArgs {
   const void *q_cos, *q_sin, *k_cos, *k_sin;
   int tbl_dtype;
   cudaStream_t stream;
+  // Optional per-sequence key lengths (clamped to kv_len, which stays the
+  // extent of the K/V tensors) and causal query offsets: with them, query row
+  // i of sequence b sits at position q_offs[b] + i and sees keys
+  // [0, min(kv_lens[b], q_offs[b] + i]) (the chunked-prefill mask).  Null: the
+  // scalar kv_len and offset 0 (both sequences aligned at 0).
+  const int32_t* kv_lens;
+  const int32_t* q_offs;
 };
 
 struct BwdArgs {
@@ -92,6 +99,10 @@ cudaError_t launch_rope_paged_write(void* q, void* k_pages, void* v_pages, const
                                     const int32_t* block_tables, const int32_t* positions,
                                     const int32_t* rope_pos, int dtype, int B, int H, int Hkv, int num_pages,
                                     int page_size, int pages_per_seq, int D, cudaStream_t stream);
+cudaError_t launch_paged_ctx_gather(const void* k_pages, const void* v_pages, const int32_t* block_tables,
+                                    const int32_t* context_lens, void* kout, void* vout, int32_t* q_offs, int L,
+                                    int B, int Hkv, int num_pages, int page_size, int pages_per_seq, int T,
+                                    int row_bytes, cudaStream_t stream);
 cudaError_t launch_paged_gather(const void* pages, const int32_t* block_tables, void* out,
                                 int dtype, int B, int Hkv, int num_pages, int page_size,
                                 int pages_per_seq, int D, cudaStream_t stream);

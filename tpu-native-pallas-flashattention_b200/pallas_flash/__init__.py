@@ -19,6 +19,7 @@ from .paged import (
     gather_paged,
     init_paged_cache,
     paged_flash_attention,
+    paged_prefill_attention,
     write_to_paged_cache,
     write_to_paged_cache_batch,
     rope_write_to_paged_cache_batch,
@@ -52,6 +53,7 @@ __all__ = [
     "flash_attention_rope",
     "rope_apply",
     "paged_flash_attention",
+    "paged_prefill_attention",
     "init_paged_cache",
     "write_to_paged_cache",
     "reference_attention",

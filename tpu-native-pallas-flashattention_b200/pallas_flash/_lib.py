@@ -60,6 +60,8 @@ _SIGNATURES = {
     "pf_paged_write": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P]),
     "pf_cache_write": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P]),
     "pf_paged_gather": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P]),
+    "pf_paged_prefill_workspace_size": (_Z, [_I, _I, _I, _I, _I]),
+    "pf_paged_prefill": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _I, _F, _P, _Z, _P]),
     "pf_rope_apply": (_I, [_P, _P, _P, _I, _P, _I, _I, _I, _I, _I, _I, _P]),
     "pf_rope_paged_write": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I,
                                  _P]),

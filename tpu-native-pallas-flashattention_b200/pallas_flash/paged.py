@@ -22,7 +22,7 @@ import torch
 
 from . import _lib
 
-__all__ = ["paged_flash_attention", "init_paged_cache", "write_to_paged_cache",
+__all__ = ["paged_flash_attention", "paged_prefill_attention", "init_paged_cache", "write_to_paged_cache",
            "write_to_paged_cache_batch", "rope_write_to_paged_cache_batch", "gather_paged"]
 
 
@@ -85,6 +85,61 @@ def paged_flash_attention(
         out.data_ptr(), _lib.dtype_code(q.dtype), batch, num_heads, num_kv_heads, num_pages,
         page_size, pages_per_seq, head_dim, max_len, float(sm_scale), ws.data_ptr(), ws.numel(),
         _lib.stream_of(q)))
+    return out
+
+
+def paged_prefill_attention(
+    q: torch.Tensor,
+    k_pages: torch.Tensor,
+    v_pages: torch.Tensor,
+    block_tables: torch.Tensor,
+    context_lens: torch.Tensor,
+    *,
+    sm_scale: Optional[float] = None,
+    max_context_len: Optional[int] = None,
+) -> torch.Tensor:
+    """Chunked prefill over a page pool (extends paged.py:102-192 from one query to L).
+
+    ``q``: ``[batch, heads, L, head_dim]``, the last L positions of every
+    sequence: row i of sequence b sits at position ``context_lens[b] - L + i``
+    and attends causally to keys ``[0, position]`` of that sequence, whose k/v
+    (including the chunk's own) are already in the pages.  Returns an array
+    shaped like ``q``.  ``max_context_len`` bounds ``context_lens`` (default:
+    the table capacity).
+    """
+    if q.ndim != 4:
+        raise ValueError(f"q must be [batch, heads, L, head_dim], got {tuple(q.shape)}")
+    if k_pages.shape != v_pages.shape:
+        raise ValueError("k_pages and v_pages must have the same shape")
+    batch, n_heads, L, head_dim = q.shape
+    num_pages, n_kv, page_size, k_head_dim = k_pages.shape
+    if k_head_dim != head_dim:
+        raise ValueError("q and pages must share head_dim")
+    if n_heads % n_kv != 0:
+        raise ValueError(f"num_heads ({n_heads}) must be a multiple of num_kv_heads ({n_kv})")
+    if block_tables.ndim != 2 or block_tables.shape[0] != batch:
+        raise ValueError(f"block_tables must be [batch, pages_per_seq], got {tuple(block_tables.shape)}")
+    if tuple(context_lens.shape) != (batch,):
+        raise ValueError(f"context_lens must be [batch], got {tuple(context_lens.shape)}")
+    if not (q.dtype == k_pages.dtype == v_pages.dtype):
+        raise ValueError("q and the page pools must share a dtype")
+    _lib.require_cuda(q, k_pages, v_pages)
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(head_dim)
+    dev = q.device
+    tables = block_tables.to(device=dev, dtype=torch.int32).contiguous()
+    lens = context_lens.to(device=dev, dtype=torch.int32).contiguous()
+    cap = tables.shape[1] * page_size
+    max_len = cap if max_context_len is None else max(1, min(int(max_context_len), cap))
+    q, k_pages, v_pages = q.contiguous(), k_pages.contiguous(), v_pages.contiguous()
+    out = torch.empty_like(q)
+    L_ = _lib.lib()
+    code = _lib.dtype_code(q.dtype)
+    ws = _lib.workspace(L_.pf_paged_prefill_workspace_size(code, batch, n_kv, max_len, head_dim), dev)
+    _lib.check(L_.pf_paged_prefill(
+        q.data_ptr(), k_pages.data_ptr(), v_pages.data_ptr(), tables.data_ptr(), lens.data_ptr(), out.data_ptr(),
+        code, batch, n_heads, n_kv, L, num_pages, page_size, tables.shape[1], head_dim, max_len, float(sm_scale),
+        ws.data_ptr(), ws.numel(), _lib.stream_of(q)))
     return out
 
 
