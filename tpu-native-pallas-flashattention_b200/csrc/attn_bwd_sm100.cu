@@ -70,6 +70,7 @@ struct BwdBars {
   uint64_t done;                   // accumulators final
   uint32_t tmem_base;
 };
+static_assert(sizeof(BwdBars) <= 256, "barrier block exceeds its shared-memory slot");
 
 // dK/dV: K, V resident; NS stages of (Q, dO) 128-row tiles plus their column statistics.
 template <int D>

@@ -65,6 +65,7 @@ struct Bars {
   uint64_t drained;     // follows every MMA of the CTA (committed after the issue loop)
   uint32_t tmem_base;
 };
+static_assert(sizeof(Bars) <= 256, "barrier block exceeds its shared-memory slot");
 
 // Eight consecutive table entries [i, i + 8) as floats (16-byte aligned).
 __device__ __forceinline__ void load8_table(const void* t, int dtype, long i, float (&o)[8]) {
