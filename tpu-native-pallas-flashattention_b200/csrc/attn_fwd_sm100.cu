@@ -62,6 +62,7 @@ struct Bars {
   uint64_t q_ready[2];  // RoPE: query tile w rotated in shared memory
   uint64_t k_full[4], v_full[4], k_empty[4], v_empty[4];
   uint64_t s_full[2], p_full[2], o_done[2];
+  uint64_t p_half[2];   // P of the first 64 keys written (PV starts on it)
   uint64_t drained;     // follows every MMA of the CTA (committed after the issue loop)
   uint32_t tmem_base;
 };
@@ -169,7 +170,8 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     mbar_init(&bars->drained, 1);
     for (int w = 0; w < 2; ++w) {
       mbar_init(&bars->s_full[w], 1);
-      mbar_init(&bars->p_full[w], kBM + 1);  // softmax threads + the data certifier
+      mbar_init(&bars->p_full[w], kBM + 1);  // softmax threads + the data certifier (K(j+1))
+      mbar_init(&bars->p_half[w], kBM + 1);  // softmax threads + the data certifier (V(j))
       mbar_init(&bars->o_done[w], 1);
     }
     fence_barrier_init();
@@ -257,18 +259,29 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         for (int kk = 1; kk < D / 16; ++kk) umma_ss_acc(dst, qd + koff<kBM>(kk), kd + koff<kBN>(kk), idesc_qk);
         umma_commit(&bars->s_full[w]);
       };
-      auto issue_pv = [&](int w, int j) {
+      // PV in two halves of the key axis: the first four k-steps start once
+      // the softmax has written P for keys [0, 64) (p_half), the rest after
+      // p_full.  Returns false if a wait gave up.
+      auto issue_pv = [&](int w, int j) -> bool {
         const uint64_t vd = desc_mn_base<kBN>(sbase + Cfg::kVOff + (j % VS) * Cfg::kTileBytes);
         const uint32_t dst = tmem + o_col[w], src = tmem + s_col[w];
+        if (!mbar_wait_spin(&bars->p_half[w], j & 1)) return false;
+        tc_fence_after();
         umma_ts(dst, src, vd, idesc_pv, j > 0 ? 1u : 0u);
 #pragma unroll
-        for (int kk = 1; kk < kBN / 16; ++kk) umma_ts_acc(dst, src + kk * 8, vd + mnoff(kk), idesc_pv);
+        for (int kk = 1; kk < kBN / 32; ++kk) umma_ts_acc(dst, src + kk * 8, vd + mnoff(kk), idesc_pv);
+        if (!mbar_wait_spin(&bars->p_full[w], j & 1)) return false;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = kBN / 32; kk < kBN / 16; ++kk) umma_ts_acc(dst, src + kk * 8, vd + mnoff(kk), idesc_pv);
         umma_commit(&bars->o_done[w]);
+        return true;
       };
-      // Tile data is certified by warp 10 inside the p_full phases: p_full[w](j)
-      // completes only once V(j) and K(j+1) are in shared memory, so apart
-      // from K(0) this thread polls nothing but the two softmax barriers (each
-      // poll it waits on costs tensor-core time).
+      // Tile data is certified by warp 10 inside the softmax barrier phases:
+      // p_half[w](j) completes only once V(j) is in shared memory and
+      // p_full[w](j) once K(j+1) is, so apart from K(0) this thread polls
+      // nothing but the softmax barriers (each poll it waits on costs
+      // tensor-core time).
       if (ok) {
         ok = mbar_wait_spin(&bars->k_full[0], 0);
         tc_fence_after();
@@ -282,11 +295,8 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         }
         if (j >= 1 && j - 1 < n_w[1]) {
           const int vp = (j - 1) % VS;
-          ok = mbar_wait_spin(&bars->p_full[1], (j - 1) & 1);
-          if (!ok) break;
           trace(3, j - 1);
-          tc_fence_after();
-          issue_pv(1, j - 1);
+          if (!(ok = issue_pv(1, j - 1))) break;
           umma_commit(&bars->v_empty[vp]);  // last reader of V_{j-1}
         }
         if (j < n_w[1]) {
@@ -295,11 +305,8 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
           umma_commit(&bars->k_empty[ks]);  // last reader of K_j
         }
         if (j < n_w[0]) {
-          ok = mbar_wait_spin(&bars->p_full[0], j & 1);
-          if (!ok) break;
           trace(6, j);
-          tc_fence_after();
-          issue_pv(0, j);
+          if (!(ok = issue_pv(0, j))) break;
           if (j >= n_w[1]) umma_commit(&bars->v_empty[vs]);
         }
       }
@@ -308,21 +315,25 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   } else if (warp == 10) {
     // --------------------------- data certifier ---------------------------
     // Adds one arrival to each softmax barrier phase once the tiles the MMA
-    // issuer will read after that phase (V(j) for PV(j), K(j+1) for the next
-    // S MMAs) have landed, then waits for the phase to complete so it never
-    // arrives twice in one phase.
+    // issuer will read after that phase (V(j) after p_half(j), K(j+1) after
+    // p_full(j)) have landed, then waits for the phases to complete so it
+    // never arrives twice in one phase.
     if (lane == 0) {
       bool ok = true;
       for (int j = 0; ok && j < n_max; ++j) {
         ok = mbar_wait(&bars->v_full[j % VS], (j / VS) & 1);
-        if (ok && j + 1 < n_max) ok = mbar_wait(&bars->k_full[(j + 1) % KS], ((j + 1) / KS) & 1);
+        if (!ok) break;
+#pragma unroll
+        for (int w = 0; w < 2; ++w)
+          if (j < n_w[w]) mbar_arrive(&bars->p_half[w]);
+        if (j + 1 < n_max) ok = mbar_wait(&bars->k_full[(j + 1) % KS], ((j + 1) / KS) & 1);
         if (!ok) break;
 #pragma unroll
         for (int w = 0; w < 2; ++w)
           if (j < n_w[w]) mbar_arrive(&bars->p_full[w]);
 #pragma unroll
         for (int w = 0; w < 2; ++w)
-          if (ok && j < n_w[w]) ok = mbar_wait(&bars->p_full[w], j & 1);
+          if (ok && j < n_w[w]) ok = mbar_wait(&bars->p_half[w], j & 1) && mbar_wait(&bars->p_full[w], j & 1);
       }
     }
   } else if (warp < 8) {
@@ -430,6 +441,11 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
           pk[i] = (fmt == 1) ? pack_bf16x2(p.x, p.y) : pack_f16x2(p.x, p.y);
         }
         tmem_st32(s_addr + c * 32, pk);
+        if (c == 0) {  // keys [0, 64) of P are in place: PV may start on them
+          tmem_wait_st();
+          tc_fence_before();
+          mbar_arrive(&bars->p_half[w]);
+        }
       }
       const float2 rs2 = add2(add2(acc[0], acc[1]), add2(acc[2], acc[3]));
       const float rowsum = rs2.x + rs2.y;
