@@ -66,6 +66,7 @@ struct BwdBars {
   uint64_t s_full[2], dp_full;     // S / dP in TMEM
   uint64_t p_ready, ds_ready;      // P / dS written for the accumulating MMAs
   uint64_t pv_done;                // dK/dV: dV(it) has read the P^T tile
+  uint64_t p_half, ds_half;        // dK/dV: the first 32-column chunk of P^T / dS written
   uint64_t s_free, dp_free;        // S (dK/dV) / dP (dQ) loaded into registers
   uint64_t done;                   // accumulators final
   uint32_t tmem_base;
@@ -200,22 +201,18 @@ __device__ __forceinline__ void load_cols(const float* src, float (&dst)[N]) {
   }
 }
 
-// Packed P for columns [col0, col0 + 32*NCH) of key row `r` into the P^T tile
-// (two 128-byte-swizzled K-major boxes of 64 columns): 16-byte chunk j of a
-// box row lives at chunk position j ^ (r % 8).
-template <int NCH>
-__device__ __forceinline__ void store_sw128_cols(uint8_t* tile, int r, int col0, const uint32_t (&pk)[NCH][16]) {
-  uint8_t* row = tile + (col0 / 64) * (128 * 128) + r * 128;
-  const int j0 = (col0 % 64) / 8;
+// Packed P of one 32-column chunk (columns [col, col + 32)) of key row `r`
+// into the P^T tile (two 128-byte-swizzled K-major boxes of 64 columns):
+// 16-byte chunk j of a box row lives at chunk position j ^ (r % 8).
+__device__ __forceinline__ void store_sw128_chunk(uint8_t* tile, int r, int col, const uint32_t (&pk)[16]) {
+  uint8_t* row = tile + (col / 64) * (128 * 128) + r * 128;
+  const int j0 = (col % 64) / 8;
 #pragma unroll
-  for (int h = 0; h < NCH; ++h)
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int j = j0 + 4 * h + q;
-      *reinterpret_cast<uint4*>(row + ((j ^ (r & 7)) << 4)) =
-          make_uint4(pk[h][4 * q], pk[h][4 * q + 1], pk[h][4 * q + 2], pk[h][4 * q + 3]);
-    }
+  for (int q = 0; q < 4; ++q)
+    *reinterpret_cast<uint4*>(row + (((j0 + q) ^ (r & 7)) << 4)) =
+        make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
 }
+
 
 // Writes an f32 accumulator row (TMEM columns [col0, col0 + n)) times `scale`
 // to a row of T, or zeros when `zero`.
@@ -297,6 +294,8 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
     mbar_init(&bars->p_ready, kEWThreads);
     mbar_init(&bars->ds_ready, kEWThreads + 1);  // + certifier: dO(it+1) landed
     mbar_init(&bars->pv_done, 1);
+    mbar_init(&bars->p_half, kEWThreads);
+    mbar_init(&bars->ds_half, kEWThreads);
     mbar_init(&bars->s_free, kEWThreads + 1);  // + certifier: Q(it+1) and its statistics landed
     mbar_init(&bars->done, 1);
     fence_barrier_init();
@@ -420,27 +419,37 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
       }
       for (int it = 0; ok && it < n_it; ++it) {
         const uint32_t q_addr = stage(it), do_addr = q_addr + Cfg::kTile;
-        // S(it+1) and dV(it) are independent; issue whichever is ready first
-        // so a late Q tile does not hold back dV (bounded like every wait).
-        bool need_s = it + 1 < n_it, need_v = true;
+        // S(it+1) and the two halves of dV(it) are independent of each other
+        // (the halves only in order); issue whichever is ready first so a
+        // late Q tile does not hold back dV (bounded like every wait).  dV's
+        // k-steps {0,1,4,5} read the first 32-column chunk each elementwise
+        // warpgroup wrote (p_half), {2,3,6,7} the second (p_ready).
+        bool need_s = it + 1 < n_it, need_v1 = true, need_v2 = true;
         const uint64_t t0 = global_timer_ns();
-        for (uint32_t spin = 1; ok && (need_s || need_v); ++spin) {
+        const uint64_t om = desc_mn_base<128>(do_addr);
+        for (uint32_t spin = 1; ok && (need_s || need_v2); ++spin) {
           if (need_s && mbar_test(&bars->s_free, it & 1)) {  // Q(it+1) certified in the phase
             trace(14, it);
             tc_fence_after();
             issue_s(it + 1);
             need_s = false;
-          } else if (need_v && mbar_test(&bars->p_ready, it & 1)) {
+          } else if (need_v1 && mbar_test(&bars->p_half, it & 1)) {
             trace(1, it);
             tc_fence_after();
-            const uint64_t om = desc_mn_base<128>(do_addr);
             umma_ss(tmem + Cfg::kDV, pd, om, idesc_acc, it > 0);
-#pragma unroll
-            for (int kk = 1; kk < 8; ++kk)
-              umma_ss_acc(tmem + Cfg::kDV, pd + koff<128>(kk), om + mnoff(kk), idesc_acc);
+            umma_ss_acc(tmem + Cfg::kDV, pd + koff<128>(1), om + mnoff(1), idesc_acc);
+            umma_ss_acc(tmem + Cfg::kDV, pd + koff<128>(4), om + mnoff(4), idesc_acc);
+            umma_ss_acc(tmem + Cfg::kDV, pd + koff<128>(5), om + mnoff(5), idesc_acc);
+            need_v1 = false;
+          } else if (!need_v1 && need_v2 && mbar_test(&bars->p_ready, it & 1)) {
+            tc_fence_after();
+            umma_ss_acc(tmem + Cfg::kDV, pd + koff<128>(2), om + mnoff(2), idesc_acc);
+            umma_ss_acc(tmem + Cfg::kDV, pd + koff<128>(3), om + mnoff(3), idesc_acc);
+            umma_ss_acc(tmem + Cfg::kDV, pd + koff<128>(6), om + mnoff(6), idesc_acc);
+            umma_ss_acc(tmem + Cfg::kDV, pd + koff<128>(7), om + mnoff(7), idesc_acc);
             umma_commit(&bars->pv_done);
             umma_commit(&bars->vempty[it % NS]);
-            need_v = false;
+            need_v2 = false;
           } else if ((spin & 1023u) == 0 && global_timer_ns() - t0 > kWaitLimitNs) {
             flag_status(PF_DEV_WAIT_TIMEOUT);
             ok = false;
@@ -448,15 +457,23 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
         }
         if (!ok) break;
         trace(2, it);
+        // dK(it) in the same two halves (ds_half, then ds_ready).
+        const uint64_t qm = desc_mn_base<128>(q_addr);
+        ok = mbar_wait_spin(&bars->ds_half, it & 1);
+        if (!ok) break;
+        tc_fence_after();
+        umma_ts(tmem + Cfg::kDK, tmem + Cfg::kDP, qm, idesc_acc, it > 0);
+        umma_ts_acc(tmem + Cfg::kDK, tmem + Cfg::kDP + split_packed_col(1), qm + mnoff(1), idesc_acc);
+        umma_ts_acc(tmem + Cfg::kDK, tmem + Cfg::kDP + split_packed_col(4), qm + mnoff(4), idesc_acc);
+        umma_ts_acc(tmem + Cfg::kDK, tmem + Cfg::kDP + split_packed_col(5), qm + mnoff(5), idesc_acc);
         ok = mbar_wait_spin(&bars->ds_ready, it & 1);
         if (!ok) break;
         trace(3, it);
         tc_fence_after();
-        const uint64_t qm = desc_mn_base<128>(q_addr);
-        umma_ts(tmem + Cfg::kDK, tmem + Cfg::kDP, qm, idesc_acc, it > 0);
-#pragma unroll
-        for (int kk = 1; kk < 8; ++kk)
-          umma_ts_acc(tmem + Cfg::kDK, tmem + Cfg::kDP + split_packed_col(kk), qm + mnoff(kk), idesc_acc);
+        umma_ts_acc(tmem + Cfg::kDK, tmem + Cfg::kDP + split_packed_col(2), qm + mnoff(2), idesc_acc);
+        umma_ts_acc(tmem + Cfg::kDK, tmem + Cfg::kDP + split_packed_col(3), qm + mnoff(3), idesc_acc);
+        umma_ts_acc(tmem + Cfg::kDK, tmem + Cfg::kDP + split_packed_col(6), qm + mnoff(6), idesc_acc);
+        umma_ts_acc(tmem + Cfg::kDK, tmem + Cfg::kDP + split_packed_col(7), qm + mnoff(7), idesc_acc);
         umma_commit(&bars->empty[it % NS]);
         if (it + 1 < n_it && !(ok = issue_dp(it + 1))) break;
         trace(4, it);
@@ -509,6 +526,9 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
         tc_fence_before();
         mbar_arrive(&bars->s_free);  // S(it+1) may now overwrite the tile
         if (tr && cw == 0) trace(5, it);
+        // Chunk by chunk: P^T of a thread's first chunk is published (p_half)
+        // before the second is computed, so dV can start on half the queries.
+        static_assert(kNCH == 2, "the two-phase P / dS publication assumes two chunks per thread");
 #pragma unroll
         for (int h = 0; h < kNCH; ++h) {
           const int q0 = qc + 32 * h;
@@ -521,13 +541,15 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
               return key_ok && qp < Sq && (!causal || qp >= kpos);
             });
           }
+          // The P^T tile is single-buffered: dV(it-1) must have read it.
+          if (h == 0 && it > 0 && !mbar_wait_spin(&bars->pv_done, (it - 1) & 1)) { ok = false; break; }
+          store_sw128_chunk(smem + Cfg::kPOff, row, col0 + 32 * h, pk[h]);
+          fence_proxy_async_smem();
+          if (h == 0) mbar_arrive(&bars->p_half);
         }
+        if (!ok) break;
         if (tr && cw == 0) trace(6, it);
       }
-      // The P^T tile is single-buffered: dV(it-1) must have read it.
-      if (it > 0 && !mbar_wait_spin(&bars->pv_done, (it - 1) & 1)) { ok = false; break; }
-      store_sw128_cols<kNCH>(smem + Cfg::kPOff, row, col0, pk);
-      fence_proxy_async_smem();
       if (tr && cw == 0) trace(7, it);
       tc_fence_before();
       mbar_arrive(&bars->p_ready);
@@ -543,6 +565,11 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
         tmem_wait_ld();
         ds_chunk_keep16<FMT>(rd, keep[h], [&](int c) { return make_float2(nd[32 * h + c], nd[32 * h + c + 1]); },
                              lane_base + Cfg::kDP + col0 + 32 * h);
+        if (h == 0) {  // first chunk of dS in place: dK may start on it
+          tmem_wait_st();
+          tc_fence_before();
+          mbar_arrive(&bars->ds_half);
+        }
       }
       tmem_wait_st();
       tc_fence_before();
