@@ -652,8 +652,7 @@ bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     mbar_init(&bars->s_full[0], 1);
     mbar_init(&bars->s_full[1], 1);
     mbar_init(&bars->dp_full, 1);
-    mbar_init(&bars->dp_free, kEWThreads + 1);   // + certifier: V(it+1) landed
-    mbar_init(&bars->ds_ready, kEWThreads + 1);  // + certifier: K(it+2) landed
+    mbar_init(&bars->ds_ready, kEWThreads + 1);  // + certifier: V(it+1) and K(it+2) landed
     mbar_init(&bars->done, 1);
     fence_barrier_init();
   }
@@ -696,12 +695,11 @@ bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       drain_ring(bars->vfull, NV, last_v);
     }
   } else if (warp == 1) {
-    // Tensor-core order per iteration:
-    //   [dP(it) in registers] dP(it+1)   [dS(it) in TMEM] dQ(it) S(it+2)
-    // S is double-buffered and dS(it) is written over the consumed S(it)
-    // tile, so the dP buffer is free as soon as the elementwise warps have
-    // loaded dP(it): dP(it+1) runs under the dS arithmetic of tile it, and
-    // S(it+2) (same buffer as S(it)) queues behind dQ(it), which reads dS(it).
+    // Tensor-core order per iteration:  [dS(it) in TMEM] dQ(it) dP(it+1) S(it+2)
+    // One poll per tile: each barrier poll the issuing thread waits on costs
+    // tensor-core time, more than overlapping dP(it+1) with the dS arithmetic
+    // of tile it gains.  S is double-buffered and dS(it) is written over the
+    // consumed S(it) tile; S(it+2) (same buffer) queues behind dQ(it).
     if (lane == 0 && n_it > 0) {
       bool ok = mbar_wait(&bars->fixed, 0);
       tc_fence_after();
@@ -735,11 +733,6 @@ bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       };
       if (ok) ok = issue_s(0) && (n_it < 2 || issue_s(1)) && issue_dp(0);
       for (int it = 0; ok && it < n_it; ++it) {
-        if (it + 1 < n_it) {
-          if (!(ok = mbar_wait_spin(&bars->dp_free, it & 1))) break;
-          tc_fence_after();
-          if (!(ok = issue_dp(it + 1))) break;
-        }
         trace(2, it);
         ok = mbar_wait_spin(&bars->ds_ready, it & 1);
         if (!ok) break;
@@ -753,6 +746,7 @@ bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         for (int kk = 1; kk < 8; ++kk)
           umma_ts_acc(tmem + Cfg::kDQ, ds_addr + split_packed_col(kk), km + mnoff(kk), idesc_acc);
         umma_commit(&bars->empty[it % NK]);
+        if (it + 1 < n_it && !(ok = issue_dp(it + 1))) break;
         if (it + 2 < n_it && !(ok = issue_s(it + 2))) break;
         trace(4, it);
       }
@@ -763,13 +757,10 @@ bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       bool ok = true;
       for (int it = 0; ok && it < n_it; ++it) {
         if (it + 1 < n_it) ok = mbar_wait(&bars->vfull[(it + 1) % NV], ((it + 1) / NV) & 1);
-        if (!ok) break;
-        mbar_arrive(&bars->dp_free);
-        if (it + 2 < n_it) ok = mbar_wait(&bars->full[(it + 2) % NK], ((it + 2) / NK) & 1);
+        if (ok && it + 2 < n_it) ok = mbar_wait(&bars->full[(it + 2) % NK], ((it + 2) / NK) & 1);
         if (!ok) break;
         mbar_arrive(&bars->ds_ready);
-        // Never arrive twice in one phase.
-        ok = mbar_wait(&bars->dp_free, it & 1) && mbar_wait(&bars->ds_ready, it & 1);
+        ok = mbar_wait(&bars->ds_ready, it & 1);  // never arrive twice in one phase
       }
     }
   } else if (warp >= 2) {
@@ -818,18 +809,14 @@ bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         uint32_t rd[kNCH][32];
         tmem_ld_cols(lane_base + Cfg::kDP + col0, rd);
         tmem_wait_ld();
-        tc_fence_before();
-        mbar_arrive(&bars->dp_free);  // dP(it+1) may now overwrite the tile
 #pragma unroll
         for (int h = 0; h < kNCH; ++h)
           ds_chunk<FMT>(rd[h], p[h], [&](int) { return ndv; }, s_addr + 32 * h);
       }
       tmem_wait_st();
       tc_fence_before();
-      // The certifier's arrival for phase it-1 waits on K(it+1); without this
-      // wait the elementwise warps could complete phase it-1 for it with
-      // their phase-it arrivals (nothing else orders them after it).
-      if (it > 0 && !mbar_wait_spin(&bars->ds_ready, (it - 1) & 1)) { ok = false; break; }
+      // Arrivals for phase it cannot run ahead: dP(it) was issued only after
+      // phase it-1 of ds_ready completed.
       mbar_arrive(&bars->ds_ready);
       if (tr) trace(10 + 3 * cw, it);
     }
