@@ -115,6 +115,10 @@ inline cudaError_t ensure_smem(K kernel, int bytes) {
   return set_smem_once(reinterpret_cast<const void*>(kernel), bytes);
 }
 
+// Streaming multiprocessors of the current device (cached per device): the
+// grid size of the persistent kernels.
+int sm_count();
+
 // Records the message returned by pf_last_error() and returns `code`.
 int set_last_error(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
 

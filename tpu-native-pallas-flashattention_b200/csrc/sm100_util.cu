@@ -4,6 +4,7 @@
 #include "kernels.h"
 
 #include <mutex>
+#include <map>
 #include <set>
 #include <utility>
 
@@ -42,6 +43,20 @@ cudaError_t set_smem_once(const void* kernel, int bytes) {
   e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
   if (e == cudaSuccess) done.insert({kernel, dev});
   return e;
+}
+
+int sm_count() {
+  static std::mutex mu;
+  static std::map<int, int> counts;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = counts.find(dev);
+  if (it != counts.end()) return it->second;
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+  counts[dev] = n;
+  return n;
 }
 
 bool make_tile_map(CUtensorMap* m, const void* base, int dtype, int D, int rows,
