@@ -600,7 +600,12 @@ cudaError_t launch_t(const FwdArgs& a, const void* k_rot) {
   cudaError_t e = ensure_smem(kern, Cfg::kSmem);
   if (e != cudaSuccess) return e;
   const int n_qtiles = (a.Sq + 2 * kBM - 1) / (2 * kBM);
-  dim3 grid((unsigned)std::min(n_qtiles * a.B * a.H, sm_count()));
+  // Persistent (one CTA per SM) when every sequence has the same length: the
+  // serpentine walk over the heaviest-first order balances the CTAs.  With
+  // per-sequence lengths (kv_lens) item costs no longer follow that order, so
+  // each item gets its own CTA and the hardware balances them as CTAs retire.
+  const int n_items = n_qtiles * a.B * a.H;
+  dim3 grid((unsigned)(a.kv_lens != nullptr ? n_items : std::min(n_items, sm_count())));
   const float scale_log2 = a.sm_scale * kLog2e;
   kern<<<grid, kThreads, Cfg::kSmem, a.stream>>>(tq, tk, tv, (T*)a.o, a.lse, a.B, a.H, a.Hkv, a.Sq,
                                                  a.kv_len, a.causal, scale_log2, n_qtiles, a.q_cos, a.q_sin,
