@@ -177,6 +177,66 @@ __global__ void bwd_preprocess_kernel(const T* __restrict__ o, const T* __restri
   if (lane == 0) delta[row] = s;
 }
 
+// Sum of the products of the 8 bf16/f16 (or 4 f32) elements packed in a and b.
+template <typename T> __device__ __forceinline__ float dot16(uint4 a, uint4 b);
+template <> __device__ __forceinline__ float dot16<float>(uint4 a, uint4 b) {
+  return __uint_as_float(a.x) * __uint_as_float(b.x) + __uint_as_float(a.y) * __uint_as_float(b.y) +
+         __uint_as_float(a.z) * __uint_as_float(b.z) + __uint_as_float(a.w) * __uint_as_float(b.w);
+}
+template <typename T2, typename F>
+__device__ __forceinline__ float dot16_packed(uint4 a, uint4 b, F to2) {
+  const unsigned av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 x = to2(*reinterpret_cast<const T2*>(&av[i])), y = to2(*reinterpret_cast<const T2*>(&bv[i]));
+    s = fmaf(x.x, y.x, fmaf(x.y, y.y, s));
+  }
+  return s;
+}
+template <> __device__ __forceinline__ float dot16<__nv_bfloat16>(uint4 a, uint4 b) {
+  return dot16_packed<__nv_bfloat162>(a, b, [](__nv_bfloat162 v) { return __bfloat1622float2(v); });
+}
+template <> __device__ __forceinline__ float dot16<__half>(uint4 a, uint4 b) {
+  return dot16_packed<__half2>(a, b, [](__half2 v) { return __half22float2(v); });
+}
+
+// The same delta with 16-byte loads: L lanes share a row (L = row bytes / 16, a power
+// of two <= 32), each lane keeps kRowsInFlight rows' loads in flight, and the grid
+// strides over rows (HBM-bound: 2 * D * elt bytes read per row).
+constexpr int kRowsInFlight = 4;
+template <typename T, int L>
+__global__ void __launch_bounds__(256)
+bwd_preprocess_vec_kernel(const uint4* __restrict__ o, const uint4* __restrict__ dout,
+                          float* __restrict__ delta, long rows) {
+  constexpr int kRowsPerWarp = 32 / L;
+  const int lane = threadIdx.x % 32, sub = lane % L;
+  const long warp = ((long)blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  const long nwarps = (long)gridDim.x * blockDim.x / 32;
+  // w0 is uniform across the warp, so every lane stays in the loop for the shuffles.
+  for (long w0 = warp * kRowsPerWarp * kRowsInFlight; w0 < rows; w0 += nwarps * kRowsPerWarp * kRowsInFlight) {
+    uint4 a[kRowsInFlight], b[kRowsInFlight];
+#pragma unroll
+    for (int u = 0; u < kRowsInFlight; ++u) {
+      const long r = w0 + u * kRowsPerWarp + lane / L;
+      if (r < rows) {
+        a[u] = __ldg(o + r * L + sub);
+        b[u] = __ldg(dout + r * L + sub);
+      } else {
+        a[u] = b[u] = make_uint4(0, 0, 0, 0);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kRowsInFlight; ++u) {
+      float s = dot16<T>(a[u], b[u]);
+#pragma unroll
+      for (int off = L / 2; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+      const long r = w0 + u * kRowsPerWarp + lane / L;
+      if (sub == 0 && r < rows) delta[r] = s;
+    }
+  }
+}
+
 // dQ: grid = (ceil(Sq / kBQ), H, B).  Outer loop over query rows, inner over
 // kv tiles, like _flash_attention_bwd_dq_kernel (:276-311).
 template <typename T, int DMAX>
@@ -420,6 +480,31 @@ cudaError_t launch_bwd_preprocess(const void* o, const void* dout, float* delta,
   const int warps = 8;
   dim3 grid((unsigned)((rows + warps - 1) / warps));
   if (rows == 0) return cudaSuccess;
+  const long row_bytes = (long)D * (dtype == PF_F32 ? 4 : 2);
+  const int L = (int)(row_bytes / 16);
+  const bool aligned = ((reinterpret_cast<uintptr_t>(o) | reinterpret_cast<uintptr_t>(dout)) % 16) == 0;
+  if (aligned && row_bytes % 16 == 0 && L >= 1 && L <= 32 && (L & (L - 1)) == 0) {
+    const int sms = sm_count();
+    const long per_block = 256 / 32 * (32 / L) * kRowsInFlight;
+    const long want = (rows + per_block - 1) / per_block;
+    const unsigned vgrid = (unsigned)(want < (long)sms * 8 ? want : (long)sms * 8);
+    const uint4* o4 = static_cast<const uint4*>(o);
+    const uint4* d4 = static_cast<const uint4*>(dout);
+#define PF_PRE_VEC(T)                                                                                   \
+  switch (L) {                                                                                          \
+    case 1: bwd_preprocess_vec_kernel<T, 1><<<vgrid, 256, 0, stream>>>(o4, d4, delta, rows); break;     \
+    case 2: bwd_preprocess_vec_kernel<T, 2><<<vgrid, 256, 0, stream>>>(o4, d4, delta, rows); break;     \
+    case 4: bwd_preprocess_vec_kernel<T, 4><<<vgrid, 256, 0, stream>>>(o4, d4, delta, rows); break;     \
+    case 8: bwd_preprocess_vec_kernel<T, 8><<<vgrid, 256, 0, stream>>>(o4, d4, delta, rows); break;     \
+    case 16: bwd_preprocess_vec_kernel<T, 16><<<vgrid, 256, 0, stream>>>(o4, d4, delta, rows); break;   \
+    default: bwd_preprocess_vec_kernel<T, 32><<<vgrid, 256, 0, stream>>>(o4, d4, delta, rows); break;   \
+  }
+    if (dtype == PF_F32) { PF_PRE_VEC(float) }
+    else if (dtype == PF_BF16) { PF_PRE_VEC(__nv_bfloat16) }
+    else { PF_PRE_VEC(__half) }
+#undef PF_PRE_VEC
+    return cudaGetLastError();
+  }
   switch (dtype) {
     case PF_F32:
       bwd_preprocess_kernel<float><<<grid, warps * 32, 0, stream>>>((const float*)o, (const float*)dout, delta, rows, D);
