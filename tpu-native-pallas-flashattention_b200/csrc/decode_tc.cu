@@ -31,6 +31,11 @@ namespace {
 constexpr int kWarps = 4;
 constexpr int kStages = 3;
 constexpr int kTileKeys = 32;
+// Page ids of one split staged in shared memory: a split spans at most 4096
+// positions (the split planner's cap) and pages hold >= 8 rows, so 513 ids
+// (+1 for a split that starts inside a page); larger spans read the table
+// from global memory instead.
+constexpr int kTblCap = 4096 / 8 + 8;
 
 template <int D>
 struct TcCfg {
@@ -40,7 +45,10 @@ struct TcCfg {
   static constexpr int kStageBytes = 2 * kOperand;
   static constexpr int kRing = kWarps * kStages * kStageBytes;
   static constexpr int kRed = kWarps * 16 * (D + 2) * 4;     // per-warp (acc, m, l), reuses the ring
-  static constexpr int kSmem = (kRing > kRed ? kRing : kRed) + kWarps * kStages * 8 + 1024;
+  static constexpr int kBarOff = kRing > kRed ? kRing : kRed;
+  static constexpr int kTblOff = kBarOff + 128;                // after the kWarps * kStages barriers
+  static constexpr int kSmem = kTblOff + kTblCap * 4 + 1024;
+  static_assert(kWarps * kStages * 8 <= 128, "barriers overlap the page-id table");
 };
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
@@ -83,7 +91,8 @@ decode_tc_kernel(DecodeArgs a, const __grid_constant__ CUtensorMap tm_k, const _
   constexpr int NB = D / 8;  // output n-blocks
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (Cfg::kRing > Cfg::kRed ? Cfg::kRing : Cfg::kRed));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kBarOff);
+  int* tbl = reinterpret_cast<int*>(smem + Cfg::kTblOff);
 
   const int split = blockIdx.x;
   const int hk = blockIdx.y / head_chunks;
@@ -102,7 +111,25 @@ decode_tc_kernel(DecodeArgs a, const __grid_constant__ CUtensorMap tm_k, const _
   }
   const int k_begin = split * a.split_len;
   const int k_end = min(len, k_begin + a.split_len);
-  if (k_begin >= k_end) return;
+  if (k_begin >= k_end) return;  // uniform over the CTA
+
+  // Paged: every page id of the split is read (and validated) once, by all
+  // threads in parallel, so the TMA issue below never waits on a global load.
+  const int p_first = paged ? k_begin / a.page_size : 0;
+  const bool tbl_smem = paged && (k_end - 1) / a.page_size - p_first + 1 <= kTblCap;
+  if (tbl_smem) {
+    const int n_ids = (k_end - 1) / a.page_size - p_first + 1;
+    const int* row_ids = a.block_tables + (long)b * a.pages_per_seq + p_first;
+    for (int i = threadIdx.x; i < n_ids; i += blockDim.x) {
+      int page = row_ids[i];
+      if (page < 0 || page >= a.num_pages) {
+        flag_status(PF_DEV_BAD_PAGE);
+        page = 0;
+      }
+      tbl[i] = page;
+    }
+    __syncthreads();
+  }
 
   uint64_t* wbar = bars + warp * kStages;
   if (lane == 0) {
@@ -154,10 +181,15 @@ decode_tc_kernel(DecodeArgs a, const __grid_constant__ CUtensorMap tm_k, const _
     mbar_expect_tx(bar, (uint32_t)(2 * nseg * seg_rows * 128 * Cfg::kBoxes));
     for (int sg = 0; sg < nseg; ++sg) {
       const int pos = kt + sg * seg_rows;
-      int page = a.block_tables[(long)b * a.pages_per_seq + pos / a.page_size];
-      if (page < 0 || page >= a.num_pages) {
-        flag_status(PF_DEV_BAD_PAGE);
-        page = 0;
+      int page;
+      if (tbl_smem) {
+        page = tbl[pos / a.page_size - p_first];
+      } else {
+        page = a.block_tables[(long)b * a.pages_per_seq + pos / a.page_size];
+        if (page < 0 || page >= a.num_pages) {
+          flag_status(PF_DEV_BAD_PAGE);
+          page = 0;
+        }
       }
       const int row = (int)(((long)page * a.Hkv + hk) * a.page_size + pos % a.page_size);
 #pragma unroll
