@@ -32,6 +32,8 @@
  *                       (the reference pages single-query decode only)
  *   pf_rope_apply       src/pallas_flash/fused_rope.py:43-50, model.py:41-67 (apply_rope; and its
  *                       inverse, for the gradient of the RoPE-fused attention)
+ *   pf_add_rms_norm     src/pallas_flash/model.py:34-38 (rms_norm) + the residual add before it
+ *   pf_silu_mul         src/pallas_flash/model.py:70-74 (the silu(gate) * up of swiglu_mlp)
  */
 #ifndef PALLAS_FLASH_B200_H_
 #define PALLAS_FLASH_B200_H_
@@ -242,6 +244,24 @@ int pf_rope_paged_write(void* q, void* k_pages, void* v_pages, const void* k,
 int pf_rope_apply(const void* x, const void* cos, const void* sin, int table_dtype,
                   void* out, int dtype, int B, int H, int S, int D, int inverse,
                   void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Decoder-block elementwise steps (the tiny-LLaMA decode step is a chain of
+ * small launches at batch 16; these fold ~8 launches per norm into one).
+ * pf_add_rms_norm: x' = x + residual (rounded to dtype; written to x_out, which
+ *   may alias x; skipped when residual is NULL, x_out then unused), then
+ *   h = (x' * rsqrt(mean(x'^2) + eps)) * weight over `rows` rows of `dim`.
+ *   Replaces rms_norm (src/pallas_flash/model.py:34-38) and the residual add
+ *   before it (model.py:120-124, 298-301).  fp32 arithmetic; roundings where
+ *   the unfused expression rounds.
+ * pf_silu_mul: out = silu(gate) * up elementwise (n elements), silu rounded to
+ *   dtype before the product -- the activation of swiglu_mlp (model.py:70-74).
+ * ------------------------------------------------------------------------- */
+int pf_add_rms_norm(const void* x, const void* residual, const void* weight,
+                    void* x_out, void* h, int dtype, long rows, int dim, float eps,
+                    void* stream);
+int pf_silu_mul(const void* gate, const void* up, void* out, int dtype, long n,
+                void* stream);
 
 #ifdef __cplusplus
 }

@@ -1,0 +1,64 @@
+"""The decoder block's fused elementwise launches against the unfused PyTorch
+expressions they replace: rms_norm (the reference's model.py:34-38) with the
+residual add before it, and the silu(gate) * up of swiglu_mlp (model.py:70-74).
+
+The residual sum must be bit-identical (both round the fp32 sum once); the norm
+may differ from the unfused form only by the order of its fp32 mean (one unit
+in the last place of the output dtype at most); silu_mul by the exp used."""
+
+import pytest
+import torch
+
+import pallas_flash as pf
+
+pytestmark = pytest.mark.gpu
+
+ULP = {torch.float32: 2e-6, torch.bfloat16: 2 ** -7, torch.float16: 2 ** -10}
+
+
+def unfused_norm(x, w, eps):
+    xf = x.to(torch.float32)
+    var = xf.square().mean(dim=-1, keepdim=True)
+    return (xf * torch.rsqrt(var + eps) * w).to(x.dtype)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("shape", [(16, 1, 512), (2, 128, 512), (3, 5, 64), (1, 1, 1000), (4, 7, 4096)])
+def test_add_rms_norm_matches_unfused(dtype, shape):
+    g = torch.Generator(device="cuda").manual_seed(shape[-1] + shape[1])
+    x = torch.randn(shape, device="cuda", generator=g).to(dtype)
+    r = torch.randn(shape, device="cuda", generator=g).to(dtype)
+    w = (1 + 0.1 * torch.randn(shape[-1], device="cuda", generator=g)).to(dtype)
+    xs, h = pf.add_rms_norm(x, r, w, 1e-5)
+    torch.testing.assert_close(xs, x + r, rtol=0, atol=0)
+    want = unfused_norm(x + r, w, 1e-5)
+    tol = ULP[dtype] * float(want.abs().max()) * 1.01
+    assert float((h.float() - want.float()).abs().max()) <= tol
+    # no residual: x passes through, h is rms_norm(x)
+    x2, h2 = pf.add_rms_norm(x, None, w, 1e-5)
+    assert x2.data_ptr() == x.data_ptr()
+    assert float((h2.float() - unfused_norm(x, w, 1e-5).float()).abs().max()) <= tol
+    assert float((pf.rms_norm(x, w, 1e-5).float() - h2.float()).abs().max()) == 0.0
+
+
+def test_add_rms_norm_zero_row_and_bad_shapes():
+    x = torch.zeros((2, 64), device="cuda", dtype=torch.bfloat16)
+    w = torch.ones(64, device="cuda", dtype=torch.bfloat16)
+    _, h = pf.add_rms_norm(x, None, w, 1e-5)
+    assert torch.count_nonzero(h) == 0
+    with pytest.raises(ValueError):
+        pf.add_rms_norm(x, None, torch.ones(63, device="cuda", dtype=torch.bfloat16), 1e-5)
+    with pytest.raises(ValueError):
+        pf.add_rms_norm(x, torch.zeros((1, 64), device="cuda", dtype=torch.bfloat16), w, 1e-5)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("n", [(16, 1, 1408), (3, 77), (1,), (2, 128, 1408)])
+def test_silu_mul_matches_unfused(dtype, n):
+    g = torch.Generator(device="cuda").manual_seed(sum(n))
+    a = (3 * torch.randn(n, device="cuda", generator=g)).to(dtype)
+    b = torch.randn(n, device="cuda", generator=g).to(dtype)
+    got = pf.silu_mul(a, b)
+    want = torch.nn.functional.silu(a) * b
+    tol = 2 * ULP[dtype] * float(want.abs().max()) + 1e-6
+    assert float((got.float() - want.float()).abs().max()) <= tol

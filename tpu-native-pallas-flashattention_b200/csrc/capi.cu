@@ -356,6 +356,23 @@ int pf_rope_apply(const void* x, const void* cos_t, const void* sin_t, int table
                      "pf_rope_apply");
 }
 
+int pf_add_rms_norm(const void* x, const void* residual, const void* weight, void* x_out, void* h, int dtype,
+                    long rows, int dim, float eps, void* stream) {
+  if (!valid_dtype(dtype) || !x || !weight || !h || (residual && !x_out))
+    return fail(PF_ERR_INVALID, "pf_add_rms_norm: bad argument");
+  if (rows < 0 || dim <= 0) return fail(PF_ERR_INVALID, "pf_add_rms_norm: shapes must be positive");
+  if (!(eps >= 0.f)) return fail(PF_ERR_INVALID, "pf_add_rms_norm: eps must be >= 0");
+  return cuda_status(launch_add_rms_norm(x, residual, weight, x_out, h, dtype, rows, dim, eps,
+                                         static_cast<cudaStream_t>(stream)),
+                     "pf_add_rms_norm");
+}
+
+int pf_silu_mul(const void* gate, const void* up, void* out, int dtype, long n, void* stream) {
+  if (!valid_dtype(dtype) || !gate || !up || !out) return fail(PF_ERR_INVALID, "pf_silu_mul: bad argument");
+  if (n < 0) return fail(PF_ERR_INVALID, "pf_silu_mul: n must be >= 0");
+  return cuda_status(launch_silu_mul(gate, up, out, dtype, n, static_cast<cudaStream_t>(stream)), "pf_silu_mul");
+}
+
 int pf_rope_paged_write(void* q, void* k_pages, void* v_pages, const void* k, const void* v, const void* cos_t,
                         const void* sin_t, int table_dtype, int table_rows, const int32_t* block_tables,
                         const int32_t* positions, const int32_t* rope_positions, int dtype, int B, int H, int Hkv,

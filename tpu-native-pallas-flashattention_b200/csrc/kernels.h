@@ -92,6 +92,9 @@ cudaError_t launch_paged_write(void* k_pages, void* v_pages, const void* k, cons
 cudaError_t launch_cache_write(void* k_cache, void* v_cache, const void* k, const void* v,
                                int dtype, int B, int Hkv, int C, int L, int D, int start,
                                cudaStream_t stream);
+cudaError_t launch_add_rms_norm(const void* x, const void* res, const void* w, void* x_out, void* h, int dtype,
+                                long rows, int dim, float eps, cudaStream_t st);
+cudaError_t launch_silu_mul(const void* g, const void* u, void* out, int dtype, long n, cudaStream_t st);
 cudaError_t launch_rope_apply(const void* x, const void* cos_t, const void* sin_t, int tdtype, void* out, int dtype,
                               long rows, int S, int D, bool inverse, cudaStream_t st);
 cudaError_t launch_rope_paged_write(void* q, void* k_pages, void* v_pages, const void* k, const void* v,

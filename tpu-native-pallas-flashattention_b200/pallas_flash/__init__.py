@@ -44,6 +44,8 @@ from .model import (
     apply_rope,
     precompute_rope,
     swiglu_mlp,
+    add_rms_norm,
+    silu_mul,
 )
 
 __all__ = [
@@ -76,6 +78,8 @@ __all__ = [
     "precompute_rope",
     "swiglu_mlp",
     # additions of this build
+    "add_rms_norm",
+    "silu_mul",
     "flash_attention_with_lse",
     "flash_attention_backward",
     "write_to_paged_cache_batch",

@@ -37,6 +37,7 @@ _P = ctypes.c_void_p
 _I = ctypes.c_int
 _F = ctypes.c_float
 _Z = ctypes.c_size_t
+_L = ctypes.c_long
 
 # name -> (restype, argtypes); mirrors include/pallas_flash_b200.h
 _SIGNATURES = {
@@ -47,6 +48,8 @@ _SIGNATURES = {
     "pf_fwd": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _F, _I, _P]),
     "pf_rope_fwd_workspace_size": (_Z, [_I, _I, _I, _I, _I]),
     "pf_rope_fwd": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _P, _I, _I, _I, _I, _I, _I, _I, _I, _F, _I, _P, _Z, _P]),
+    "pf_add_rms_norm": (_I, [_P, _P, _P, _P, _P, _I, _L, _I, _F, _P]),
+    "pf_silu_mul": (_I, [_P, _P, _P, _I, _L, _P]),
     "pf_bwd_preprocess": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _P]),
     "pf_bwd_dq": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _F, _I, _P]),
     "pf_bwd_dkv": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _F, _I, _P]),

@@ -37,11 +37,36 @@ Cache = list  # per-layer list of {"k": [b, n_kv, cache_size, d], "v": same}
 # --------------------------------------------------------------------------- #
 # Building blocks (model.py:34-74)
 # --------------------------------------------------------------------------- #
+def add_rms_norm(x: torch.Tensor, residual: Optional[torch.Tensor], weight: torch.Tensor,
+                 eps: float):
+    """``x' = x + residual`` (``x' = x`` when ``residual`` is None) and ``rms_norm(x')``, as
+    ``(x', h)`` from one kernel launch (``pf_add_rms_norm``).  The sum is rounded to
+    ``x.dtype`` as the unfused ``x + residual`` rounds it; the norm follows model.py:34-38
+    in fp32 (``weight`` is taken in ``x.dtype``)."""
+    _lib.require_cuda(x, weight)
+    dim = x.shape[-1]
+    if weight.numel() != dim:
+        raise ValueError(f"norm weight has {weight.numel()} elements, expected {dim}")
+    xc = x.contiguous()
+    w = weight.to(x.dtype).contiguous()
+    h = torch.empty_like(xc)
+    if residual is None:
+        x_out, r = xc, None
+    else:
+        if residual.shape != x.shape:
+            raise ValueError(f"residual shape {tuple(residual.shape)} != x shape {tuple(x.shape)}")
+        r = residual.to(x.dtype).contiguous()
+        x_out = torch.empty_like(xc)
+    _lib.check(_lib.lib().pf_add_rms_norm(xc.data_ptr(), _lib.ptr(r), w.data_ptr(),
+                                          x_out.data_ptr() if r is not None else None, h.data_ptr(),
+                                          _lib.dtype_code(x.dtype), xc.numel() // dim, dim, float(eps),
+                                          _lib.stream_of(x)))
+    return x_out, h
+
+
 def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
-    """Root-mean-square layer norm (LLaMA-style, no mean subtraction)."""
-    xf = x.to(torch.float32)
-    var = xf.square().mean(dim=-1, keepdim=True)
-    return (xf * torch.rsqrt(var + eps) * weight).to(x.dtype)
+    """Root-mean-square layer norm (LLaMA-style, no mean subtraction), one kernel launch."""
+    return add_rms_norm(x, None, weight, eps)[1]
 
 
 def precompute_rope(seq_len: int, head_dim: int, theta: float, device=None):
@@ -64,9 +89,22 @@ def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.T
     return x * cos[None, None] + _rotate_half(x) * sin[None, None]
 
 
+def silu_mul(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """``silu(gate) * up`` in one launch (``pf_silu_mul``); silu is rounded to the tensor
+    dtype before the product, as in the unfused expression."""
+    _lib.require_cuda(gate, up)
+    if gate.shape != up.shape or gate.dtype != up.dtype:
+        raise ValueError("silu_mul: gate and up must have the same shape and dtype")
+    g, u = gate.contiguous(), up.contiguous()
+    out = torch.empty_like(g)
+    _lib.check(_lib.lib().pf_silu_mul(g.data_ptr(), u.data_ptr(), out.data_ptr(), _lib.dtype_code(g.dtype),
+                                      g.numel(), _lib.stream_of(g)))
+    return out
+
+
 def swiglu_mlp(x, w_gate, w_up, w_down):
     """SwiGLU feed-forward: ``(silu(x W_gate) * (x W_up)) W_down``."""
-    return (torch.nn.functional.silu(x @ w_gate) * (x @ w_up)) @ w_down
+    return silu_mul(x @ w_gate, x @ w_up) @ w_down
 
 
 _ROPE_CACHE: Dict[tuple, tuple] = {}
@@ -111,8 +149,7 @@ def decoder_block(params: Params, x, cos, sin, cfg: ModelConfig, interpret: bool
     k = apply_rope(k, cos, sin)
     attn = flash_attention(q, k, v, causal=True, block_q=cfg.block_q, block_k=cfg.block_k)
     attn = attn.transpose(1, 2).reshape(batch, seq, cfg.dim)
-    x = x + attn @ params["wo"]
-    h = rms_norm(x, params["ffn_norm"], cfg.rms_norm_eps)
+    x, h = add_rms_norm(x, attn @ params["wo"], params["ffn_norm"], cfg.rms_norm_eps)
     return x + swiglu_mlp(h, params["w_gate"], params["w_up"], params["w_down"])
 
 
@@ -223,17 +260,18 @@ def prefill(params: Params, tokens, cfg: ModelConfig, interpret: bool = False,
     x = params["embed"][tokens]
     cos, sin = _rope_slice(0, seq, cfg, x.dtype, x.device)
     cache = init_kv_cache(cfg, batch, cache_size, x.dtype, x.device)
+    mlp = None  # each block's MLP output is added by the next norm's launch
     for idx, layer in enumerate(params["layers"]):
-        h = rms_norm(x, layer["attn_norm"], cfg.rms_norm_eps)
+        x, h = add_rms_norm(x, mlp, layer["attn_norm"], cfg.rms_norm_eps)
         q, k, v = project_qkv(layer, h, cfg)
         q = apply_rope(q, cos, sin)
         k = apply_rope(k, cos, sin)
-        x = x + _attend(layer, q, k, v, cfg, interpret, causal=True)
         _cache_write(cache[idx], k, v, 0)
-        h = rms_norm(x, layer["ffn_norm"], cfg.rms_norm_eps)
-        x = x + swiglu_mlp(h, layer["w_gate"], layer["w_up"], layer["w_down"])
-    x = rms_norm(x, params["final_norm"], cfg.rms_norm_eps)
-    return x @ params["lm_head"], cache
+        x, h = add_rms_norm(x, _attend(layer, q, k, v, cfg, interpret, causal=True), layer["ffn_norm"],
+                            cfg.rms_norm_eps)
+        mlp = swiglu_mlp(h, layer["w_gate"], layer["w_up"], layer["w_down"])
+    x, h = add_rms_norm(x, mlp, params["final_norm"], cfg.rms_norm_eps)
+    return h @ params["lm_head"], cache
 
 
 def _decode_layers(params: Params, token, cache: Cache, pos: int, slot: int, kv_len: int,
@@ -246,18 +284,19 @@ def _decode_layers(params: Params, token, cache: Cache, pos: int, slot: int, kv_
     table = torch.arange(batch, dtype=torch.int32, device=x.device).reshape(batch, 1)
     slots = torch.full((batch,), slot, dtype=torch.int32, device=x.device)
     rows = torch.zeros((batch,), dtype=torch.int32, device=x.device)
+    mlp = None  # each block's MLP output is added by the next norm's launch
     for layer, layer_cache in zip(params["layers"], cache):
-        h = rms_norm(x, layer["attn_norm"], cfg.rms_norm_eps)
+        x, h = add_rms_norm(x, mlp, layer["attn_norm"], cfg.rms_norm_eps)
         q, k, v = project_qkv(layer, h, cfg)
         q = rope_write_to_paged_cache_batch(q, k, v, layer_cache["k"], layer_cache["v"], cos, sin, table,
                                             slots, rows)
         attn = flash_attention_decode(q, layer_cache["k"], layer_cache["v"], kv_len,
                                       block_k=cfg.block_k)
-        x = x + attn.transpose(1, 2).reshape(batch, 1, cfg.dim) @ layer["wo"]
-        h = rms_norm(x, layer["ffn_norm"], cfg.rms_norm_eps)
-        x = x + swiglu_mlp(h, layer["w_gate"], layer["w_up"], layer["w_down"])
-    x = rms_norm(x, params["final_norm"], cfg.rms_norm_eps)
-    return x @ params["lm_head"], cache
+        x, h = add_rms_norm(x, attn.transpose(1, 2).reshape(batch, 1, cfg.dim) @ layer["wo"],
+                            layer["ffn_norm"], cfg.rms_norm_eps)
+        mlp = swiglu_mlp(h, layer["w_gate"], layer["w_up"], layer["w_down"])
+    x, h = add_rms_norm(x, mlp, params["final_norm"], cfg.rms_norm_eps)
+    return h @ params["lm_head"], cache
 
 
 def decode_step(params: Params, token, cache: Cache, pos: int, cfg: ModelConfig,
@@ -306,17 +345,18 @@ class DecodeGraph:
         self.rope_rows.copy_(self.pos.to(torch.int32).expand_as(self.rope_rows))
         x = p["embed"][self.token]
         batch = x.shape[0]
+        mlp = None
         for layer, lc in zip(p["layers"], self.cache):
-            h = rms_norm(x, layer["attn_norm"], cfg.rms_norm_eps)
+            x, h = add_rms_norm(x, mlp, layer["attn_norm"], cfg.rms_norm_eps)
             q, k, v = project_qkv(layer, h, cfg)
             q = rope_write_to_paged_cache_batch(q, k, v, lc["k"], lc["v"], self.cos, self.sin, self.table,
                                                 self.slots, self.rope_rows)
             attn = paged_flash_attention(q, lc["k"], lc["v"], self.table, self.lens, max_context_len=self.C)
-            x = x + attn.transpose(1, 2).reshape(batch, 1, cfg.dim) @ layer["wo"]
-            h = rms_norm(x, layer["ffn_norm"], cfg.rms_norm_eps)
-            x = x + swiglu_mlp(h, layer["w_gate"], layer["w_up"], layer["w_down"])
-        x = rms_norm(x, p["final_norm"], cfg.rms_norm_eps)
-        self.token.copy_(_argmax_last(x @ p["lm_head"]))
+            x, h = add_rms_norm(x, attn.transpose(1, 2).reshape(batch, 1, cfg.dim) @ layer["wo"],
+                                layer["ffn_norm"], cfg.rms_norm_eps)
+            mlp = swiglu_mlp(h, layer["w_gate"], layer["w_up"], layer["w_down"])
+        x, h = add_rms_norm(x, mlp, p["final_norm"], cfg.rms_norm_eps)
+        self.token.copy_(_argmax_last(h @ p["lm_head"]))
         self.pos.add_(1)
 
     def capture(self, token, pos: int, last_pos: int):
@@ -403,17 +443,18 @@ def prefill_ring(params: Params, tokens, cfg: ModelConfig, capacity: int,
     keep = min(seq, capacity)
     start = seq - keep
     cache = init_ring_cache(cfg, batch, capacity, x.dtype, x.device)
+    mlp = None  # each block's MLP output is added by the next norm's launch
     for idx, layer in enumerate(params["layers"]):
-        h = rms_norm(x, layer["attn_norm"], cfg.rms_norm_eps)
+        x, h = add_rms_norm(x, mlp, layer["attn_norm"], cfg.rms_norm_eps)
         q, k, v = project_qkv(layer, h, cfg)
         q = apply_rope(q, cos, sin)
         k = apply_rope(k, cos, sin)
-        x = x + _attend(layer, q, k, v, cfg, interpret, causal=True)
         _cache_write(cache[idx], k[:, :, start:], v[:, :, start:], start)
-        h = rms_norm(x, layer["ffn_norm"], cfg.rms_norm_eps)
-        x = x + swiglu_mlp(h, layer["w_gate"], layer["w_up"], layer["w_down"])
-    x = rms_norm(x, params["final_norm"], cfg.rms_norm_eps)
-    return x @ params["lm_head"], cache
+        x, h = add_rms_norm(x, _attend(layer, q, k, v, cfg, interpret, causal=True), layer["ffn_norm"],
+                            cfg.rms_norm_eps)
+        mlp = swiglu_mlp(h, layer["w_gate"], layer["w_up"], layer["w_down"])
+    x, h = add_rms_norm(x, mlp, params["final_norm"], cfg.rms_norm_eps)
+    return h @ params["lm_head"], cache
 
 
 def ring_decode_step(params: Params, token, cache: Cache, pos: int, cfg: ModelConfig,
