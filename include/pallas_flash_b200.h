@@ -34,6 +34,8 @@
  *                       inverse, for the gradient of the RoPE-fused attention)
  *   pf_add_rms_norm     src/pallas_flash/model.py:34-38 (rms_norm) + the residual add before it
  *   pf_silu_mul         src/pallas_flash/model.py:70-74 (the silu(gate) * up of swiglu_mlp)
+ *   pf_decode_positions src/pallas_flash/model.py:434-449, 475-476 (slot, kv_len and RoPE row
+ *                       of a decode step, computed on the device)
  */
 #ifndef PALLAS_FLASH_B200_H_
 #define PALLAS_FLASH_B200_H_
@@ -254,14 +256,24 @@ int pf_rope_apply(const void* x, const void* cos, const void* sin, int table_dty
  *   Replaces rms_norm (src/pallas_flash/model.py:34-38) and the residual add
  *   before it (model.py:120-124, 298-301).  fp32 arithmetic; roundings where
  *   the unfused expression rounds.
- * pf_silu_mul: out = silu(gate) * up elementwise (n elements), silu rounded to
- *   dtype before the product -- the activation of swiglu_mlp (model.py:70-74).
+ * pf_silu_mul: out[r, c] = silu(gate[r, c]) * up[r, c] over rows x cols, silu
+ *   rounded to dtype before the product -- the activation of swiglu_mlp
+ *   (model.py:70-74).  gate/up rows are in_stride elements apart (>= cols), so
+ *   both halves of one fused [rows, 2*cols] projection can be passed; out is
+ *   contiguous [rows, cols].
+ * pf_decode_positions: for a decode step at p = *pos (int64, device), writes
+ *   slots[b] = p % capacity, lens[b] = min(p + 1, capacity), rope_rows[b] = p
+ *   for b < B, then *pos = p + 1 -- the per-step slot / live-length / RoPE-row
+ *   arithmetic of model.py:434-449, 475-476, on the device so that one
+ *   captured decode step serves every position.
  * ------------------------------------------------------------------------- */
 int pf_add_rms_norm(const void* x, const void* residual, const void* weight,
                     void* x_out, void* h, int dtype, long rows, int dim, float eps,
                     void* stream);
-int pf_silu_mul(const void* gate, const void* up, void* out, int dtype, long n,
-                void* stream);
+int pf_silu_mul(const void* gate, const void* up, void* out, int dtype, long rows,
+                int cols, long in_stride, void* stream);
+int pf_decode_positions(int64_t* pos, int capacity, int32_t* slots, int32_t* lens,
+                        int32_t* rope_rows, int B, void* stream);
 
 #ifdef __cplusplus
 }

@@ -62,3 +62,43 @@ def test_silu_mul_matches_unfused(dtype, n):
     want = torch.nn.functional.silu(a) * b
     tol = 2 * ULP[dtype] * float(want.abs().max()) + 1e-6
     assert float((got.float() - want.float()).abs().max()) <= tol
+
+
+def test_silu_mul_on_a_fused_projection_equals_separate_halves():
+    g = torch.Generator(device="cuda").manual_seed(3)
+    gu = torch.randn((16, 1, 2 * 1408), device="cuda", generator=g).to(torch.bfloat16)
+    fused = pf.silu_mul(gu)
+    split = pf.silu_mul(gu[..., :1408].contiguous(), gu[..., 1408:].contiguous())
+    assert fused.shape == (16, 1, 1408)
+    torch.testing.assert_close(fused, split, rtol=0, atol=0)
+
+
+def test_swiglu_mlp_with_fused_projection_tracks_weight_updates():
+    from pallas_flash import model
+    g = torch.Generator(device="cuda").manual_seed(4)
+    x = torch.randn((16, 1, 512), device="cuda", generator=g).to(torch.bfloat16)
+    wg, wu = (0.05 * torch.randn((512, 1408), device="cuda", generator=g)).to(torch.bfloat16), \
+             (0.05 * torch.randn((512, 1408), device="cuda", generator=g)).to(torch.bfloat16)
+    wd = (0.05 * torch.randn((1408, 512), device="cuda", generator=g)).to(torch.bfloat16)
+    want = (torch.nn.functional.silu(x @ wg) * (x @ wu)) @ wd
+    got = model.swiglu_mlp(x, wg, wu, wd)
+    assert float((got.float() - want.float()).abs().max()) <= 0.02 * float(want.abs().max())
+    wu.mul_(2.0)  # in-place update: the cached concatenation must not be reused
+    want2 = (torch.nn.functional.silu(x @ wg) * (x @ wu)) @ wd
+    got2 = model.swiglu_mlp(x, wg, wu, wd)
+    assert float((got2.float() - want2.float()).abs().max()) <= 0.02 * float(want2.abs().max())
+
+
+@pytest.mark.parametrize("pos,C", [(0, 512), (511, 512), (512, 512), (4222, 512), (7, 1)])
+def test_decode_positions(pos, C):
+    from pallas_flash import _lib
+    B = 16
+    p = torch.tensor([pos], dtype=torch.long, device="cuda")
+    slots, lens, rows = (torch.full((B,), -1, dtype=torch.int32, device="cuda") for _ in range(3))
+    _lib.check(_lib.lib().pf_decode_positions(p.data_ptr(), C, slots.data_ptr(), lens.data_ptr(),
+                                              rows.data_ptr(), B, _lib.stream_of(p)))
+    torch.cuda.synchronize()
+    assert int(p.item()) == pos + 1
+    assert slots.tolist() == [pos % C] * B
+    assert lens.tolist() == [min(pos + 1, C)] * B
+    assert rows.tolist() == [pos] * B

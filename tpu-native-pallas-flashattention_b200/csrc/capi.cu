@@ -367,10 +367,21 @@ int pf_add_rms_norm(const void* x, const void* residual, const void* weight, voi
                      "pf_add_rms_norm");
 }
 
-int pf_silu_mul(const void* gate, const void* up, void* out, int dtype, long n, void* stream) {
+int pf_silu_mul(const void* gate, const void* up, void* out, int dtype, long rows, int cols, long in_stride,
+                void* stream) {
   if (!valid_dtype(dtype) || !gate || !up || !out) return fail(PF_ERR_INVALID, "pf_silu_mul: bad argument");
-  if (n < 0) return fail(PF_ERR_INVALID, "pf_silu_mul: n must be >= 0");
-  return cuda_status(launch_silu_mul(gate, up, out, dtype, n, static_cast<cudaStream_t>(stream)), "pf_silu_mul");
+  if (rows < 0 || cols < 0 || in_stride < cols) return fail(PF_ERR_INVALID, "pf_silu_mul: bad shape");
+  return cuda_status(launch_silu_mul(gate, up, out, dtype, rows, cols, in_stride, static_cast<cudaStream_t>(stream)),
+                     "pf_silu_mul");
+}
+
+int pf_decode_positions(int64_t* pos, int capacity, int32_t* slots, int32_t* lens, int32_t* rope_rows, int B,
+                        void* stream) {
+  if (!pos || !slots || !lens || !rope_rows) return fail(PF_ERR_INVALID, "pf_decode_positions: bad argument");
+  if (capacity <= 0 || B <= 0) return fail(PF_ERR_INVALID, "pf_decode_positions: capacity and B must be positive");
+  return cuda_status(launch_decode_positions(pos, capacity, slots, lens, rope_rows, B,
+                                             static_cast<cudaStream_t>(stream)),
+                     "pf_decode_positions");
 }
 
 int pf_rope_paged_write(void* q, void* k_pages, void* v_pages, const void* k, const void* v, const void* cos_t,

@@ -94,7 +94,10 @@ cudaError_t launch_cache_write(void* k_cache, void* v_cache, const void* k, cons
                                cudaStream_t stream);
 cudaError_t launch_add_rms_norm(const void* x, const void* res, const void* w, void* x_out, void* h, int dtype,
                                 long rows, int dim, float eps, cudaStream_t st);
-cudaError_t launch_silu_mul(const void* g, const void* u, void* out, int dtype, long n, cudaStream_t st);
+cudaError_t launch_silu_mul(const void* g, const void* u, void* out, int dtype, long rows, int cols, long in_stride,
+                            cudaStream_t st);
+cudaError_t launch_decode_positions(int64_t* pos, int C, int32_t* slots, int32_t* lens, int32_t* rope_rows, int B,
+                                    cudaStream_t st);
 cudaError_t launch_rope_apply(const void* x, const void* cos_t, const void* sin_t, int tdtype, void* out, int dtype,
                               long rows, int S, int D, bool inverse, cudaStream_t st);
 cudaError_t launch_rope_paged_write(void* q, void* k_pages, void* v_pages, const void* k, const void* v,

@@ -21,6 +21,7 @@ Differences that keep behaviour but suit the GPU:
 
 from __future__ import annotations
 
+import weakref
 from typing import Any, Dict, List, Optional
 
 import torch
@@ -89,22 +90,59 @@ def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.T
     return x * cos[None, None] + _rotate_half(x) * sin[None, None]
 
 
-def silu_mul(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+def silu_mul(gate: torch.Tensor, up: Optional[torch.Tensor] = None) -> torch.Tensor:
     """``silu(gate) * up`` in one launch (``pf_silu_mul``); silu is rounded to the tensor
-    dtype before the product, as in the unfused expression."""
-    _lib.require_cuda(gate, up)
-    if gate.shape != up.shape or gate.dtype != up.dtype:
-        raise ValueError("silu_mul: gate and up must have the same shape and dtype")
-    g, u = gate.contiguous(), up.contiguous()
-    out = torch.empty_like(g)
-    _lib.check(_lib.lib().pf_silu_mul(g.data_ptr(), u.data_ptr(), out.data_ptr(), _lib.dtype_code(g.dtype),
-                                      g.numel(), _lib.stream_of(g)))
+    dtype before the product, as in the unfused expression.  With ``up`` None, ``gate``
+    is one fused ``[..., 2F]`` projection whose halves are the gate and the up values."""
+    _lib.require_cuda(gate)
+    if up is None:
+        g = gate.contiguous()
+        cols = g.shape[-1] // 2
+        if g.shape[-1] != 2 * cols:
+            raise ValueError("silu_mul: a fused projection must have an even last dimension")
+        gp, up_ptr, stride = g.data_ptr(), g.data_ptr() + cols * g.element_size(), 2 * cols
+        out_shape = (*g.shape[:-1], cols)
+    else:
+        _lib.require_cuda(up)
+        if gate.shape != up.shape or gate.dtype != up.dtype:
+            raise ValueError("silu_mul: gate and up must have the same shape and dtype")
+        g, u = gate.contiguous(), up.contiguous()
+        cols = g.shape[-1]
+        gp, up_ptr, stride = g.data_ptr(), u.data_ptr(), cols
+        out_shape = g.shape
+    out = torch.empty(out_shape, dtype=g.dtype, device=g.device)
+    rows = out.numel() // cols if cols else 0
+    _lib.check(_lib.lib().pf_silu_mul(gp, up_ptr, out.data_ptr(), _lib.dtype_code(g.dtype), rows, cols, stride,
+                                      _lib.stream_of(g)))
     return out
 
 
+# Column-concatenated copies of weight matrices, so that projections sharing an
+# input run as one matmul.  An entry is used only while every source tensor is
+# alive (weak references) and unmodified (its version counter): the cache never
+# changes results, only the launch count.
+_FUSED: Dict[tuple, tuple] = {}
+
+
+def _fused_columns(*ws: torch.Tensor) -> torch.Tensor:
+    key = tuple(id(w) for w in ws)
+    hit = _FUSED.get(key)
+    if hit is not None:
+        refs, versions, fused = hit
+        if all(r() is w for r, w in zip(refs, ws)) and versions == tuple(w._version for w in ws):
+            return fused
+    if len(_FUSED) > 512:
+        for k in [k for k, (refs, _, _) in _FUSED.items() if any(r() is None for r in refs)]:
+            del _FUSED[k]
+    fused = torch.cat(ws, dim=1)
+    _FUSED[key] = (tuple(weakref.ref(w) for w in ws), tuple(w._version for w in ws), fused)
+    return fused
+
+
 def swiglu_mlp(x, w_gate, w_up, w_down):
-    """SwiGLU feed-forward: ``(silu(x W_gate) * (x W_up)) W_down``."""
-    return silu_mul(x @ w_gate, x @ w_up) @ w_down
+    """SwiGLU feed-forward: ``(silu(x W_gate) * (x W_up)) W_down``; the two input
+    projections run as one matmul over ``[W_gate | W_up]``."""
+    return silu_mul(x @ _fused_columns(w_gate, w_up)) @ w_down
 
 
 _ROPE_CACHE: Dict[tuple, tuple] = {}
@@ -340,9 +378,10 @@ class DecodeGraph:
 
     def _step(self):
         cfg, p = self.cfg, self.params
-        self.slots.copy_((self.pos % self.C).to(torch.int32).expand_as(self.slots))
-        self.lens.copy_(torch.clamp(self.pos + 1, max=self.C).to(torch.int32).expand_as(self.lens))
-        self.rope_rows.copy_(self.pos.to(torch.int32).expand_as(self.rope_rows))
+        # slot pos % C, live length min(pos + 1, C), RoPE row pos; then pos += 1
+        _lib.check(_lib.lib().pf_decode_positions(self.pos.data_ptr(), self.C, self.slots.data_ptr(),
+                                                  self.lens.data_ptr(), self.rope_rows.data_ptr(),
+                                                  self.slots.numel(), _lib.stream_of(self.pos)))
         x = p["embed"][self.token]
         batch = x.shape[0]
         mlp = None
@@ -357,7 +396,6 @@ class DecodeGraph:
             mlp = swiglu_mlp(h, layer["w_gate"], layer["w_up"], layer["w_down"])
         x, h = add_rms_norm(x, mlp, p["final_norm"], cfg.rms_norm_eps)
         self.token.copy_(_argmax_last(h @ p["lm_head"]))
-        self.pos.add_(1)
 
     def capture(self, token, pos: int, last_pos: int):
         """One eager warm-up step at ``pos`` (it writes cache slot ``pos`` with the values the
