@@ -28,6 +28,8 @@
  *   pf_paged_gather     src/pallas_flash/paged.py:158-159            (the block-table index map)
  *   pf_rope_paged_write src/pallas_flash/model.py:338-342 + paged.py:205-223 (RoPE of the decode
  *                       token's q/k fused with the k/v page write)
+ *   pf_rope_paged_write_qkv  the same, reading q/k/v from one fused projection row
+ *                       (model.py:80-88 project_qkv as a single matmul)
  *   pf_paged_prefill    extension of src/pallas_flash/paged.py:102-192 to an L-query chunk
  *                       (the reference pages single-query decode only)
  *   pf_rope_apply       src/pallas_flash/fused_rope.py:43-50, model.py:41-67 (apply_rope; and its
@@ -234,6 +236,18 @@ int pf_rope_paged_write(void* q, void* k_pages, void* v_pages, const void* k,
                         const int32_t* positions, const int32_t* rope_positions,
                         int dtype, int B, int H, int Hkv, int num_pages, int page_size,
                         int pages_per_seq, int D, void* stream);
+
+/* pf_rope_paged_write_qkv: pf_rope_paged_write on the output of one fused
+ *   q/k/v projection: row b of qkv (row_stride elements apart, >= (H+2*Hkv)*D)
+ *   holds sequence b's H query heads, then its Hkv key heads, then its Hkv
+ *   value heads, D elements each.  Rotated q goes to q_out [B, H, 1, D]
+ *   (contiguous, not aliasing qkv); rotated k and v go to the pages as above.
+ */
+int pf_rope_paged_write_qkv(const void* qkv, long row_stride, void* q_out, void* k_pages,
+                            void* v_pages, const void* cos, const void* sin, int table_dtype,
+                            int table_rows, const int32_t* block_tables, const int32_t* positions,
+                            const int32_t* rope_positions, int dtype, int B, int H, int Hkv,
+                            int num_pages, int page_size, int pages_per_seq, int D, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Rotary embedding.

@@ -258,6 +258,31 @@ def test_rope_paged_write_matches_unfused(dtype, H, Hkv, D, ps):
     assert np.array_equal(widen(vp), vp_want)  # v and every untouched slot byte-exact
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("H,Hkv,D,ps", [(8, 2, 64, 16), (4, 4, 128, 8)])
+def test_rope_paged_write_qkv_equals_separate_tensors(dtype, H, Hkv, D, ps):
+    """One fused projection row per sequence (q heads, k heads, v heads) gives
+    byte-identical q and pages to the separate-tensor entry point."""
+    B, pps, rows = 5, 6, 100
+    num_pages = B * pps + 3
+    rng = np.random.default_rng(8)
+    qkv = to_dev(randn((B, 1, (H + 2 * Hkv) * D), 11), dtype)
+    q = qkv[..., :H * D].reshape(B, 1, H, D).transpose(1, 2).contiguous()
+    k = qkv[..., H * D:(H + Hkv) * D].reshape(B, 1, Hkv, D).transpose(1, 2).contiguous()
+    v = qkv[..., (H + Hkv) * D:].reshape(B, 1, Hkv, D).transpose(1, 2).contiguous()
+    cos, sin = pf.precompute_rope(rows, D, 10000.0, device="cuda")
+    tables = torch.from_numpy(rng.permutation(num_pages)[: B * pps].reshape(B, pps).astype(np.int32))
+    positions = torch.from_numpy(rng.integers(0, pps * ps, size=B).astype(np.int32))
+    rope_rows = torch.from_numpy(rng.integers(0, rows, size=B).astype(np.int32))
+    kp0, vp0 = to_dev(randn((num_pages, Hkv, ps, D), 12), dtype), to_dev(randn((num_pages, Hkv, ps, D), 13), dtype)
+    kp1, vp1, kp2, vp2 = kp0.clone(), vp0.clone(), kp0.clone(), vp0.clone()
+    want = pf.rope_write_to_paged_cache_batch(q, k, v, kp1, vp1, cos, sin, tables, positions, rope_rows)
+    got = pf.rope_write_to_paged_cache_qkv(qkv, H, kp2, vp2, cos, sin, tables, positions, rope_rows)
+    assert got.shape == (B, H, 1, D) and got.is_contiguous()
+    assert torch.equal(got, want)
+    assert torch.equal(kp2, kp1) and torch.equal(vp2, vp1)
+
+
 # --------------------------------------------------------------------------
 # Paged (chunked) prefill -- an extension: the reference pages single-query
 # decode only.  Oracle: the chunk's L queries are the last rows of a causal

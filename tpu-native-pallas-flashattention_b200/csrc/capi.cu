@@ -396,10 +396,38 @@ int pf_rope_paged_write(void* q, void* k_pages, void* v_pages, const void* k, co
     return fail(PF_ERR_INVALID, "pf_rope_paged_write: shapes must be positive");
   if (D % 2 != 0 || D > 1024) return fail(PF_ERR_INVALID, "pf_rope_paged_write: head_dim must be even and <= 1024");
   if (H % Hkv != 0) return fail(PF_ERR_INVALID, "pf_rope_paged_write: num_heads must be a multiple of num_kv_heads");
-  return cuda_status(launch_rope_paged_write(q, k_pages, v_pages, k, v, cos_t, sin_t, table_dtype, table_rows,
-                                             block_tables, positions, rope_positions, dtype, B, H, Hkv, num_pages,
-                                             page_size, pages_per_seq, D, static_cast<cudaStream_t>(stream)),
+  return cuda_status(launch_rope_paged_write(q, (long)H * D, q, k_pages, v_pages, k, v, (long)Hkv * D, cos_t, sin_t,
+                                             table_dtype, table_rows, block_tables, positions, rope_positions, dtype,
+                                             B, H, Hkv, num_pages, page_size, pages_per_seq, D,
+                                             static_cast<cudaStream_t>(stream)),
                      "pf_rope_paged_write");
+}
+
+int pf_rope_paged_write_qkv(const void* qkv, long row_stride, void* q_out, void* k_pages, void* v_pages,
+                            const void* cos_t, const void* sin_t, int table_dtype, int table_rows,
+                            const int32_t* block_tables, const int32_t* positions, const int32_t* rope_positions,
+                            int dtype, int B, int H, int Hkv, int num_pages, int page_size, int pages_per_seq, int D,
+                            void* stream) {
+  if (!valid_dtype(dtype) || !valid_dtype(table_dtype) || !qkv || !q_out || !k_pages || !v_pages || !cos_t ||
+      !sin_t || !block_tables || !positions || !rope_positions)
+    return fail(PF_ERR_INVALID, "pf_rope_paged_write_qkv: bad argument");
+  if (B <= 0 || H <= 0 || Hkv <= 0 || num_pages <= 0 || page_size <= 0 || pages_per_seq <= 0 || D <= 0 ||
+      table_rows <= 0)
+    return fail(PF_ERR_INVALID, "pf_rope_paged_write_qkv: shapes must be positive");
+  if (D % 2 != 0 || D > 1024)
+    return fail(PF_ERR_INVALID, "pf_rope_paged_write_qkv: head_dim must be even and <= 1024");
+  if (H % Hkv != 0)
+    return fail(PF_ERR_INVALID, "pf_rope_paged_write_qkv: num_heads must be a multiple of num_kv_heads");
+  if (row_stride < (long)(H + 2 * Hkv) * D)
+    return fail(PF_ERR_INVALID, "pf_rope_paged_write_qkv: row_stride %ld < (H + 2*Hkv) * D", row_stride);
+  const size_t elt = dtype_size(dtype);
+  const char* base = static_cast<const char*>(qkv);
+  return cuda_status(launch_rope_paged_write(qkv, row_stride, q_out, k_pages, v_pages, base + (size_t)H * D * elt,
+                                             base + (size_t)(H + Hkv) * D * elt, row_stride, cos_t, sin_t,
+                                             table_dtype, table_rows, block_tables, positions, rope_positions, dtype,
+                                             B, H, Hkv, num_pages, page_size, pages_per_seq, D,
+                                             static_cast<cudaStream_t>(stream)),
+                     "pf_rope_paged_write_qkv");
 }
 
 size_t pf_paged_prefill_workspace_size(int dtype, int B, int Hkv, int max_context_len, int D) {

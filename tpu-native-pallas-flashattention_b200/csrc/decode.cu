@@ -340,21 +340,26 @@ __global__ void paged_write_kernel(T* kp, T* vp, const T* k, const T* v, const i
 // y = x*cos + rotate_half(x)*sin in fp32 with one rounding; an out-of-range
 // page (or logical page, or table row) is clamped like the page write above.
 // grid = (H + Hkv, B), block = D/2 threads (one rotation pair each).
+// Sequence b's q heads start at q_in + b * q_bs (written to q_out, contiguous
+// [B, H, D]; q_out may equal q_in when q_bs = H * D), its k / v heads at
+// k / v + b * kv_bs: separate tensors, or the slices of one fused projection row.
 template <typename T>
-__global__ void rope_paged_write_kernel(T* q, T* kp, T* vp, const T* k, const T* v, const void* cos_t,
-                                        const void* sin_t, int tdtype, int table_rows, const int32_t* tables,
-                                        const int32_t* positions, const int32_t* rope_pos, int H, int Hkv,
-                                        int num_pages, int ps, int pages_per_seq, int D) {
+__global__ void rope_paged_write_kernel(const T* q_in, long q_bs, T* q_out, T* kp, T* vp, const T* k, const T* v,
+                                        long kv_bs, const void* cos_t, const void* sin_t, int tdtype,
+                                        int table_rows, const int32_t* tables, const int32_t* positions,
+                                        const int32_t* rope_pos, int H, int Hkv, int num_pages, int ps,
+                                        int pages_per_seq, int D) {
   const int b = blockIdx.y, head = blockIdx.x, i = threadIdx.x, half = D / 2;
   if (i >= half) return;
   const long r = min(max(rope_pos[b], 0), table_rows - 1);
   const float c1 = load_any(cos_t, tdtype, r * D + i), s1 = load_any(sin_t, tdtype, r * D + i);
   const float c2 = load_any(cos_t, tdtype, r * D + i + half), s2 = load_any(sin_t, tdtype, r * D + i + half);
   if (head < H) {
-    T* x = q + ((long)b * H + head) * D;
+    const T* x = q_in + (long)b * q_bs + (long)head * D;
+    T* y = q_out + ((long)b * H + head) * D;
     const float x1 = to_f(x[i]), x2 = to_f(x[i + half]);
-    x[i] = from_f<T>(x1 * c1 - x2 * s1);
-    x[i + half] = from_f<T>(x2 * c2 + x1 * s2);
+    y[i] = from_f<T>(x1 * c1 - x2 * s1);
+    y[i + half] = from_f<T>(x2 * c2 + x1 * s2);
     return;
   }
   const int hk = head - H;
@@ -364,7 +369,7 @@ __global__ void rope_paged_write_kernel(T* q, T* kp, T* vp, const T* k, const T*
   int page = tables[(long)b * pages_per_seq + lp];
   page = min(max(page, 0), num_pages - 1);
   const long dst = (((long)page * Hkv + hk) * ps + off) * D;
-  const long src = ((long)b * Hkv + hk) * D;
+  const long src = (long)b * kv_bs + (long)hk * D;
   const float x1 = to_f(k[src + i]), x2 = to_f(k[src + i + half]);
   kp[dst + i] = from_f<T>(x1 * c1 - x2 * s1);
   kp[dst + i + half] = from_f<T>(x2 * c2 + x1 * s2);
@@ -508,18 +513,19 @@ cudaError_t launch_paged_ctx_gather(const void* k_pages, const void* v_pages, co
   return cudaGetLastError();
 }
 
-cudaError_t launch_rope_paged_write(void* q, void* k_pages, void* v_pages, const void* k, const void* v,
-                                    const void* cos_t, const void* sin_t, int tdtype, int table_rows,
-                                    const int32_t* block_tables, const int32_t* positions,
-                                    const int32_t* rope_pos, int dtype, int B, int H, int Hkv, int num_pages,
-                                    int page_size, int pages_per_seq, int D, cudaStream_t stream) {
+cudaError_t launch_rope_paged_write(const void* q_in, long q_bs, void* q_out, void* k_pages, void* v_pages,
+                                    const void* k, const void* v, long kv_bs, const void* cos_t, const void* sin_t,
+                                    int tdtype, int table_rows, const int32_t* block_tables,
+                                    const int32_t* positions, const int32_t* rope_pos, int dtype, int B, int H,
+                                    int Hkv, int num_pages, int page_size, int pages_per_seq, int D,
+                                    cudaStream_t stream) {
   const dim3 grid(H + Hkv, B);
   const int th = ((D / 2 + 31) / 32) * 32;
-#define PF_RPW(T)                                                                                              \
-  rope_paged_write_kernel<T><<<grid, th, 0, stream>>>((T*)q, (T*)k_pages, (T*)v_pages, (const T*)k,             \
-                                                      (const T*)v, cos_t, sin_t, tdtype, table_rows,            \
-                                                      block_tables, positions, rope_pos, H, Hkv, num_pages,     \
-                                                      page_size, pages_per_seq, D)
+#define PF_RPW(T)                                                                                               \
+  rope_paged_write_kernel<T><<<grid, th, 0, stream>>>((const T*)q_in, q_bs, (T*)q_out, (T*)k_pages, (T*)v_pages, \
+                                                      (const T*)k, (const T*)v, kv_bs, cos_t, sin_t, tdtype,     \
+                                                      table_rows, block_tables, positions, rope_pos, H, Hkv,     \
+                                                      num_pages, page_size, pages_per_seq, D)
   if (dtype == PF_F32) PF_RPW(float);
   else if (dtype == PF_BF16) PF_RPW(__nv_bfloat16);
   else PF_RPW(__half);

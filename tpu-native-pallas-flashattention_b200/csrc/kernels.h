@@ -100,11 +100,12 @@ cudaError_t launch_decode_positions(int64_t* pos, int C, int32_t* slots, int32_t
                                     cudaStream_t st);
 cudaError_t launch_rope_apply(const void* x, const void* cos_t, const void* sin_t, int tdtype, void* out, int dtype,
                               long rows, int S, int D, bool inverse, cudaStream_t st);
-cudaError_t launch_rope_paged_write(void* q, void* k_pages, void* v_pages, const void* k, const void* v,
-                                    const void* cos_t, const void* sin_t, int tdtype, int table_rows,
-                                    const int32_t* block_tables, const int32_t* positions,
-                                    const int32_t* rope_pos, int dtype, int B, int H, int Hkv, int num_pages,
-                                    int page_size, int pages_per_seq, int D, cudaStream_t stream);
+cudaError_t launch_rope_paged_write(const void* q_in, long q_bs, void* q_out, void* k_pages, void* v_pages,
+                                    const void* k, const void* v, long kv_bs, const void* cos_t, const void* sin_t,
+                                    int tdtype, int table_rows, const int32_t* block_tables,
+                                    const int32_t* positions, const int32_t* rope_pos, int dtype, int B, int H,
+                                    int Hkv, int num_pages, int page_size, int pages_per_seq, int D,
+                                    cudaStream_t stream);
 cudaError_t launch_paged_ctx_gather(const void* k_pages, const void* v_pages, const int32_t* block_tables,
                                     const int32_t* context_lens, void* kout, void* vout, int32_t* q_offs, int L,
                                     int B, int Hkv, int num_pages, int page_size, int pages_per_seq, int T,

@@ -23,6 +23,7 @@ from .paged import (
     write_to_paged_cache,
     write_to_paged_cache_batch,
     rope_write_to_paged_cache_batch,
+    rope_write_to_paged_cache_qkv,
 )
 from .reference import reference_attention
 from .model import (
@@ -84,6 +85,7 @@ __all__ = [
     "flash_attention_backward",
     "write_to_paged_cache_batch",
     "rope_write_to_paged_cache_batch",
+    "rope_write_to_paged_cache_qkv",
     "gather_paged",
 ]
 

@@ -69,6 +69,8 @@ _SIGNATURES = {
     "pf_rope_apply": (_I, [_P, _P, _P, _I, _P, _I, _I, _I, _I, _I, _I, _P]),
     "pf_rope_paged_write": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I,
                                  _P]),
+    "pf_rope_paged_write_qkv": (_I, [_P, _L, _P, _P, _P, _P, _P, _I, _I, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I,
+                                     _I, _P]),
 }
 
 EXPORTED = tuple(_SIGNATURES)

@@ -29,7 +29,7 @@ import torch
 from . import _lib
 from .config import ModelConfig
 from .flash_attention import flash_attention, flash_attention_decode
-from .paged import paged_flash_attention, rope_write_to_paged_cache_batch
+from .paged import paged_flash_attention, rope_write_to_paged_cache_qkv
 
 Params = Dict[str, Any]
 Cache = list  # per-layer list of {"k": [b, n_kv, cache_size, d], "v": same}
@@ -325,9 +325,9 @@ def _decode_layers(params: Params, token, cache: Cache, pos: int, slot: int, kv_
     mlp = None  # each block's MLP output is added by the next norm's launch
     for layer, layer_cache in zip(params["layers"], cache):
         x, h = add_rms_norm(x, mlp, layer["attn_norm"], cfg.rms_norm_eps)
-        q, k, v = project_qkv(layer, h, cfg)
-        q = rope_write_to_paged_cache_batch(q, k, v, layer_cache["k"], layer_cache["v"], cos, sin, table,
-                                            slots, rows)
+        qkv = h @ _fused_columns(layer["wq"], layer["wk"], layer["wv"])  # one projection matmul
+        q = rope_write_to_paged_cache_qkv(qkv, cfg.n_heads, layer_cache["k"], layer_cache["v"], cos, sin, table,
+                                          slots, rows)
         attn = flash_attention_decode(q, layer_cache["k"], layer_cache["v"], kv_len,
                                       block_k=cfg.block_k)
         x, h = add_rms_norm(x, attn.transpose(1, 2).reshape(batch, 1, cfg.dim) @ layer["wo"],
@@ -387,9 +387,9 @@ class DecodeGraph:
         mlp = None
         for layer, lc in zip(p["layers"], self.cache):
             x, h = add_rms_norm(x, mlp, layer["attn_norm"], cfg.rms_norm_eps)
-            q, k, v = project_qkv(layer, h, cfg)
-            q = rope_write_to_paged_cache_batch(q, k, v, lc["k"], lc["v"], self.cos, self.sin, self.table,
-                                                self.slots, self.rope_rows)
+            qkv = h @ _fused_columns(layer["wq"], layer["wk"], layer["wv"])
+            q = rope_write_to_paged_cache_qkv(qkv, cfg.n_heads, lc["k"], lc["v"], self.cos, self.sin, self.table,
+                                              self.slots, self.rope_rows)
             attn = paged_flash_attention(q, lc["k"], lc["v"], self.table, self.lens, max_context_len=self.C)
             x, h = add_rms_norm(x, attn.transpose(1, 2).reshape(batch, 1, cfg.dim) @ layer["wo"],
                                 layer["ffn_norm"], cfg.rms_norm_eps)

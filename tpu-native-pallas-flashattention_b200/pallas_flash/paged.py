@@ -218,6 +218,40 @@ def rope_write_to_paged_cache_batch(q, k, v, k_pages, v_pages, cos, sin, block_t
     return q
 
 
+def rope_write_to_paged_cache_qkv(qkv, num_heads: int, k_pages, v_pages, cos, sin, block_tables, positions,
+                                  rope_positions):
+    """``rope_write_to_paged_cache_batch`` on one fused projection: ``qkv`` is
+    ``[batch, 1, (num_heads + 2 * num_kv_heads) * head_dim]`` (q heads, then k heads, then v
+    heads, as ``h @ [W_q | W_k | W_v]`` gives them).  Returns the rotated q as a new
+    ``[batch, num_heads, 1, head_dim]`` tensor; k and v land in the pages.  One launch, no
+    split/copy of the projection."""
+    _lib.require_cuda(qkv, k_pages, v_pages, cos, sin)
+    num_pages, n_kv, page_size, head_dim = k_pages.shape
+    batch = qkv.shape[0]
+    width = (num_heads + 2 * n_kv) * head_dim
+    if qkv.dim() != 3 or qkv.shape[1] != 1 or qkv.shape[2] != width:
+        raise ValueError(f"qkv must be [batch, 1, {width}] for {num_heads}/{n_kv} heads of {head_dim}")
+    if qkv.dtype != k_pages.dtype:
+        raise ValueError("qkv and the page pools must have the same dtype")
+    if tuple(cos.shape) != tuple(sin.shape) or cos.shape[1] != head_dim:
+        raise ValueError(f"cos/sin must be [rows, {head_dim}]")
+    if not (k_pages.is_contiguous() and v_pages.is_contiguous()):
+        raise ValueError("page pools must be contiguous to be written in place")
+    dev = k_pages.device
+    tables = torch.as_tensor(block_tables, dtype=torch.int32, device=dev).reshape(batch, -1).contiguous()
+    pos = torch.as_tensor(positions, dtype=torch.int32, device=dev).reshape(batch).contiguous()
+    rpos = torch.as_tensor(rope_positions, dtype=torch.int32, device=dev).reshape(batch).contiguous()
+    src = qkv.contiguous()
+    q = torch.empty((batch, num_heads, 1, head_dim), dtype=qkv.dtype, device=dev)
+    sin = sin.to(cos.dtype)
+    _lib.check(_lib.lib().pf_rope_paged_write_qkv(
+        src.data_ptr(), width, q.data_ptr(), k_pages.data_ptr(), v_pages.data_ptr(),
+        cos.contiguous().data_ptr(), sin.contiguous().data_ptr(), _lib.dtype_code(cos.dtype), cos.shape[0],
+        tables.data_ptr(), pos.data_ptr(), rpos.data_ptr(), _lib.dtype_code(q.dtype), batch, num_heads, n_kv,
+        num_pages, page_size, tables.shape[1], head_dim, _lib.stream_of(src)))
+    return q
+
+
 def write_to_paged_cache(k_pages, v_pages, k, v, block_table, position: int):
     """Write one token's K/V into the page holding ``position`` (paged.py:205-223).
 
