@@ -324,6 +324,37 @@ def test_paged_prefill_matches_oracle(dtype, H, Hkv, D, ps, lens, L):
     assert np.max(np.abs(to_np(got) - want)) < tol
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_paged_prefill_reads_no_ungathered_workspace_row(dtype):
+    """The gather writes only rows below each context's next 128-row boundary; the
+    workspace is NaN-poisoned first, so a prefill kernel reading any row past that
+    would put NaN in the output.  Very unequal contexts leave most rows unwritten."""
+    from pallas_flash import _lib
+    H, Hkv, D, ps, L = 4, 2, 128, 16, 32
+    lens = [1500, 33, 200, 129]
+    B = len(lens)
+    pps = max((n + ps - 1) // ps for n in lens) + 1
+    num_pages = B * pps + 5
+    tables = scrambled_table(B, pps, num_pages, seed=9)
+    q, kp, vp = randn((B, H, L, D), 51), randn((num_pages, Hkv, ps, D), 52), randn((num_pages, Hkv, ps, D), 53)
+    tq, tk, tv = to_dev(q, dtype), to_dev(kp, dtype), to_dev(vp, dtype)
+    lib, code = _lib.lib(), _lib.dtype_code(dtype)
+    cap = pps * ps
+    ws = torch.empty(lib.pf_paged_prefill_workspace_size(code, B, Hkv, cap, D), dtype=torch.uint8, device="cuda")
+    ws.view(torch.int32).fill_(-1)  # all-ones bit patterns: NaN in f32 and bf16 alike
+    ttab = torch.from_numpy(tables).cuda()
+    tlen = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    out = torch.empty_like(tq)
+    _lib.check(lib.pf_paged_prefill(tq.data_ptr(), tk.data_ptr(), tv.data_ptr(), ttab.data_ptr(), tlen.data_ptr(),
+                                    out.data_ptr(), code, B, H, Hkv, L, num_pages, ps, pps, D, cap,
+                                    1.0 / np.sqrt(D), ws.data_ptr(), ws.numel(), _lib.stream_of(tq)))
+    got = to_np(out)
+    assert np.isfinite(got).all()
+    want = _prefill_oracle(widen(tq), widen(tk), widen(tv), tables, lens)
+    tol = 2e-3 if dtype == torch.float32 else 2e-2
+    assert np.max(np.abs(got - want)) < tol
+
+
 def test_paged_prefill_single_token_equals_paged_decode():
     """L = 1 is the decode case: same math as paged_flash_attention (different kernels)."""
     B, H, Hkv, D, ps = 3, 8, 2, 128, 16

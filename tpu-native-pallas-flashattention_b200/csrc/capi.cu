@@ -451,6 +451,9 @@ int pf_paged_prefill(const void* q, const void* k_pages, const void* v_pages, co
   if (row_bytes % 16 != 0)
     return fail(PF_ERR_UNSUPPORTED, "pf_paged_prefill: head_dim * element size must be a multiple of 16 bytes");
   const int T = max_context_len < pages_per_seq * page_size ? max_context_len : pages_per_seq * page_size;
+  if ((long)T * (row_bytes / 16) >= (1l << 31))
+    return fail(PF_ERR_UNSUPPORTED, "pf_paged_prefill: context of %d rows x %d bytes exceeds 2^31 16-byte words", T,
+                row_bytes);
   const size_t need = pf_paged_prefill_workspace_size(dtype, B, Hkv, T, D);
   if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))
     return fail(PF_ERR_WORKSPACE, "pf_paged_prefill: workspace of %zu bytes required, got %zu", need,

@@ -378,26 +378,33 @@ __global__ void rope_paged_write_kernel(const T* q_in, long q_bs, T* q_out, T* k
 }
 
 // Paged prefill, step 1: the context of every sequence as contiguous rows
-// [B, Hkv, T, D] (T = the longest context), rows at or past context_lens[b]
-// zero (the attention masks them, and zeros keep 0 * V finite), plus the
-// causal offsets q_offs[b] = context_lens[b] - L of the L-query chunk.
-// 16-byte words; an out-of-range page is flagged and read as page 0.
+// [B, Hkv, T, D] (T = the longest context) plus the causal offsets
+// q_offs[b] = context_lens[b] - L of the L-query chunk.  Only the rows the
+// attention can load are produced: [0, context_lens[b]) from the pages and
+// zeros up to the next 128-row tile boundary (the last tile is read whole;
+// zeros keep 0 * V finite there).  Later rows are never loaded: every
+// prefill kernel stops at the sequence's key length.  grid.x = B * Hkv
+// planes, grid.y = chunks of a plane's 16-byte words (32-bit index math);
+// an out-of-range page is flagged and read as page 0.
+constexpr int kGatherTile = 128;
 __global__ void paged_ctx_gather_kernel(const uint4* __restrict__ kpages, const uint4* __restrict__ vpages,
                                         const int32_t* __restrict__ tables, const int32_t* __restrict__ ctx,
                                         uint4* __restrict__ kout, uint4* __restrict__ vout, int32_t* q_offs,
                                         int L, int B, int Hkv, int num_pages, int ps, int pps, int T, int vec) {
-  if (blockIdx.x == 0)
+  if (blockIdx.x == 0 && blockIdx.y == 0)
     for (int b = threadIdx.x; b < B; b += blockDim.x) q_offs[b] = ctx[b] - L;
-  const long total = (long)B * Hkv * T * vec;
-  for (long idx = blockIdx.x * (long)blockDim.x + threadIdx.x; idx < total; idx += (long)gridDim.x * blockDim.x) {
-    const int c = (int)(idx % vec);
-    const long rowi = idx / vec;          // over (b, hk, t)
-    const int t = (int)(rowi % T);
-    const long plane = rowi / T;          // b * Hkv + hk
-    const int b = (int)(plane / Hkv), hk = (int)(plane % Hkv);
+  const int plane = blockIdx.x, b = plane / Hkv, hk = plane % Hkv;
+  const int len = max(0, min(min(ctx[b], T), pps * ps));                  // rows with data
+  const int lim = min(T, (max(0, min(ctx[b], T)) + kGatherTile - 1) / kGatherTile * kGatherTile);
+  const int total = lim * vec;
+  const int32_t* trow = tables + (long)b * pps;
+  uint4* ko = kout + (long)plane * T * vec;
+  uint4* vo = vout + (long)plane * T * vec;
+  for (int w = blockIdx.y * blockDim.x + threadIdx.x; w < total; w += gridDim.y * blockDim.x) {
+    const int t = w / vec, c = w - t * vec;
     uint4 kw = make_uint4(0, 0, 0, 0), vw = kw;
-    if (t < ctx[b] && t < pps * ps) {
-      int page = tables[(long)b * pps + t / ps];
+    if (t < len) {
+      int page = trow[t / ps];
       if (page < 0 || page >= num_pages) {
         flag_status(PF_DEV_BAD_PAGE);
         page = 0;
@@ -406,8 +413,8 @@ __global__ void paged_ctx_gather_kernel(const uint4* __restrict__ kpages, const 
       kw = kpages[src];
       vw = vpages[src];
     }
-    kout[idx] = kw;
-    vout[idx] = vw;
+    ko[w] = kw;
+    vo[w] = vw;
   }
 }
 
@@ -504,10 +511,17 @@ cudaError_t launch_paged_ctx_gather(const void* k_pages, const void* v_pages, co
                                     int B, int Hkv, int num_pages, int page_size, int pages_per_seq, int T,
                                     int row_bytes, cudaStream_t stream) {
   const int vec = row_bytes / 16;
-  const long total = (long)B * Hkv * T * vec;
-  const long want = (total + 255) / 256;
-  const int blocks = (int)(want < 148L * 32 ? (want > 0 ? want : 1) : 148L * 32);
-  paged_ctx_gather_kernel<<<blocks, 256, 0, stream>>>((const uint4*)k_pages, (const uint4*)v_pages, block_tables,
+  const long planes = (long)B * Hkv;
+  if (planes <= 0) return cudaSuccess;
+  // ~8 words per thread, and enough blocks over all planes to fill the GPU.
+  const long per_plane = (long)T * vec;
+  long chunks = (per_plane + 256 * 8 - 1) / (256 * 8);
+  const long min_chunks = ((long)sm_count() * 8 + planes - 1) / planes;
+  if (chunks < min_chunks) chunks = min(min_chunks, (per_plane + 255) / 256);
+  if (chunks < 1) chunks = 1;
+  if (chunks > 65535) chunks = 65535;
+  const dim3 grid((unsigned)planes, (unsigned)chunks);
+  paged_ctx_gather_kernel<<<grid, 256, 0, stream>>>((const uint4*)k_pages, (const uint4*)v_pages, block_tables,
                                                       context_lens, (uint4*)kout, (uint4*)vout, q_offs, L, B, Hkv,
                                                       num_pages, page_size, pages_per_seq, T, vec);
   return cudaGetLastError();
