@@ -452,7 +452,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-extras", action="store_true", help="skip the secondary workloads and CPU baseline")
-    ap.add_argument("--mode", choices=["bench", "profile-c2", "profile-decode"], default="bench",
+    ap.add_argument("--mode", choices=["bench", "profile-c2", "profile-decode", "profile-gen"], default="bench",
                     help="profile-*: only launch the kernels of one workload (for ncu captures)")
     args = ap.parse_args()
 
@@ -495,6 +495,18 @@ def main():
     if args.mode == "profile-decode":
         # config-4 shape on 32 sequences (~2.4 GB of KV): warmup + steps decode calls
         paged_decode_bench(pf, dev, iters=args.steps, n_seqs=32, warmup=args.warmup)
+        torch.cuda.synchronize()
+        print(json.dumps({"mode": args.mode, "ok": True}))
+        return
+    if args.mode == "profile-gen":
+        # config-5 model: ring-streaming generation of `steps` tokens after a short warm-up run
+        cfg = pf.ModelConfig(vocab_size=32000, dim=512, n_layers=8, n_heads=8, n_kv_heads=2, head_dim=64,
+                             ffn_hidden=1408, rope_theta=10000.0, rms_norm_eps=1e-5)
+        params = pf.init_params(0, cfg, dtype=torch.bfloat16, device=dev)
+        g = torch.Generator(device=dev).manual_seed(0)
+        prompts = torch.randint(0, 32000, (16, 128), device=dev, generator=g)
+        pf.generate_streaming(params, prompts, max(2, args.warmup), cfg, window=512)
+        pf.generate_streaming(params, prompts, args.steps, cfg, window=512)
         torch.cuda.synchronize()
         print(json.dumps({"mode": args.mode, "ok": True}))
         return
