@@ -22,9 +22,11 @@ is the total FLOP of all ranks / that time.
 Also reported (rank 0, N = 1 only): the paged-decode HBM bandwidth on the
 config-4 workload (256 sequences, kv_len ~ U[512, 32768], page 16, H32/Hkv8,
 D128) and the CPU baseline -- the oracle's numpy restatement of the reference
-timed on one (batch, kv-head group) unit of config 2 and scaled by the unit count.
-``--impl reference`` times that CPU restatement alone (the reference is JAX on
-TPU; JAX is not installed, so its own CPU path cannot run here).
+timed on one query head of one (batch, kv-head group) unit of config 2 and scaled
+by FLOP.  ``--impl reference`` times that CPU restatement alone, one such head per
+step (at most one untimed warm-up head; timed steps stop after 150 s, so any K
+ends within minutes) -- the reference is JAX on TPU; JAX is not installed, so its
+own CPU path cannot run here.
 """
 
 from __future__ import annotations
@@ -131,29 +133,37 @@ def cpu_sample_step(q, k, v, do):
     return out
 
 
-def cpu_baseline(steps: int = 1, warmup: int = 0):
+def cpu_baseline(steps: int = 1, warmup: int = 0, budget_s: float = 150.0):
+    """The oracle's fp32 numpy restatement of the reference's XLA-CPU path on a bounded
+    sample: each step is one query head of one (batch, kv-head group) unit of config 2
+    (1/128 of the step's work, ~3 s on 16 host threads), scaled by FLOP.  Timed steps
+    stop early once `budget_s` has elapsed, so any --steps keeps the run to minutes."""
     rng = np.random.default_rng(0)
-    g = H // HKV
-    q = rng.standard_normal((1, g, S, D), dtype=np.float32)
+    q = rng.standard_normal((1, 1, S, D), dtype=np.float32)
     k = rng.standard_normal((1, 1, S, D), dtype=np.float32)
     v = rng.standard_normal((1, 1, S, D), dtype=np.float32)
-    do = rng.standard_normal((1, g, S, D), dtype=np.float32)
+    do = rng.standard_normal((1, 1, S, D), dtype=np.float32)
     # All host threads for the BLAS the oracle's numpy matmuls run on (torchrun
     # sets OMP_NUM_THREADS=1, which would otherwise pin it to one core).
     from threadpoolctl import threadpool_info, threadpool_limits
     with threadpool_limits(limits=os.cpu_count() or 1, user_api="blas"):
         cores = max([i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"] or [1])
-        for _ in range(warmup):
+        for _ in range(max(0, warmup)):
             cpu_sample_step(q, k, v, do)
         t0 = time.perf_counter()
-        for _ in range(steps):
+        done = 0
+        for _ in range(max(1, steps)):
             cpu_sample_step(q, k, v, do)
-        dt = (time.perf_counter() - t0) / steps
-    unit_flop = STEP_FLOP / UNITS
-    return {"value": unit_flop / dt / 1e12, "unit": "TFLOP/s", "cores": cores,
+            done += 1
+            if time.perf_counter() - t0 > budget_s:
+                break
+        dt = (time.perf_counter() - t0) / done
+    head_flop = STEP_FLOP / (B * H)
+    return {"value": head_flop / dt / 1e12, "unit": "TFLOP/s", "cores": cores,
             "kind": "port",
-            "sample": f"1 of {UNITS} (batch, kv-head group) units of config 2 (4 q heads x 4096 x 128, causal), "
-                      f"numpy fp32 naive fwd + closed-form VJP, {dt:.2f} s/unit, scaled by unit FLOP"}
+            "sample": f"1 query head of 1 of {UNITS} (batch, kv-head group) units of config 2 (4096 x 128, "
+                      f"causal), numpy fp32 naive fwd + closed-form VJP, {dt:.2f} s per head, scaled by FLOP; "
+                      f"{done} timed step(s)"}
 
 
 # --------------------------------------------------------------------------- GPU side
@@ -468,8 +478,7 @@ def main():
         if rank != 0:
             return
         t0 = time.perf_counter()
-        cpu_baseline(steps=max(0, args.warmup))
-        cb = cpu_baseline(steps=args.steps)
+        cb = cpu_baseline(steps=args.steps, warmup=min(1, max(0, args.warmup)))
         print(json.dumps({
             "impl": "reference", "metric": "fwd+bwd attention TFLOP/s", "value": cb["value"], "unit": "TFLOP/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
