@@ -620,7 +620,7 @@ def main():
         line["c1_forward"] = c1_forward_bench(pf, dev)
         line["paged_prefill"] = paged_prefill_bench(pf, dev)
         line["generation"] = generation_bench(pf, dev)
-        line["cpu_baseline"] = cpu_baseline(steps=1)
+        line["cpu_baseline"] = cpu_baseline(steps=4)  # ~10-15 s of host work
     if rank == 0:
         print(json.dumps(line))
     if world > 1:
