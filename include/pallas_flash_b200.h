@@ -38,6 +38,8 @@
  *   pf_silu_mul         src/pallas_flash/model.py:70-74 (the silu(gate) * up of swiglu_mlp)
  *   pf_decode_positions src/pallas_flash/model.py:434-449, 475-476 (slot, kv_len and RoPE row
  *                       of a decode step, computed on the device)
+ *   pf_argmax_embed     src/pallas_flash/model.py:377-383, 520-528 (greedy argmax) + :333, 478
+ *                       (the next step's embedding lookup)
  */
 #ifndef PALLAS_FLASH_B200_H_
 #define PALLAS_FLASH_B200_H_
@@ -288,6 +290,15 @@ int pf_silu_mul(const void* gate, const void* up, void* out, int dtype, long row
                 int cols, long in_stride, void* stream);
 int pf_decode_positions(int64_t* pos, int capacity, int32_t* slots, int32_t* lens,
                         int32_t* rope_rows, int B, void* stream);
+/* pf_argmax_embed: the end of a greedy decode step.  For each of `rows` rows of
+ *   logits (row_stride elements apart, `vocab` used): token[b] (int64) = the
+ *   first index of the row's maximum, a NaN ranking above every number (the
+ *   argmax rule of jnp.argmax at model.py:377-383, 520-528); then, when embed
+ *   [vocab_rows, dim] is not NULL, x[b, :] = embed[token[b], :], the next
+ *   step's input (the embedding lookup of model.py:333, 478).
+ */
+int pf_argmax_embed(const void* logits, long row_stride, int vocab, int rows, int64_t* token,
+                    const void* embed, void* x, int dim, int dtype, void* stream);
 
 #ifdef __cplusplus
 }

@@ -102,3 +102,32 @@ def test_decode_positions(pos, C):
     assert slots.tolist() == [pos % C] * B
     assert lens.tolist() == [min(pos + 1, C)] * B
     assert rows.tolist() == [pos] * B
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+def test_argmax_embed_matches_torch_argmax_and_lookup(dtype):
+    from pallas_flash import _lib
+    rows, vocab, dim = 6, 32000, 512
+    g = torch.Generator(device="cuda").manual_seed(5)
+    logits = torch.randn((rows, vocab), device="cuda", generator=g).to(dtype)
+    logits[1, 100] = logits[1, 31000] = 1e4         # tie: the first index wins
+    logits[2] = float("-inf")                        # all -inf: index 0
+    logits[3, 7] = float("nan")                      # NaN ranks above every number
+    logits[3, 9] = 1e4
+    logits[4, 5] = logits[4, 6] = float("nan")       # first NaN
+    logits[5, vocab - 1] = 1e4                       # the last column
+    embed = torch.randn((vocab, dim), device="cuda", generator=g).to(dtype)
+    token = torch.full((rows, 1), -1, dtype=torch.long, device="cuda")
+    x = torch.zeros((rows, 1, dim), dtype=dtype, device="cuda")
+    _lib.check(_lib.lib().pf_argmax_embed(logits.data_ptr(), vocab, vocab, rows, token.data_ptr(), embed.data_ptr(),
+                                          x.data_ptr(), dim, _lib.dtype_code(dtype), _lib.stream_of(logits)))
+    want = torch.argmax(logits, dim=-1, keepdim=True)
+    assert token.tolist() == want.tolist()
+    assert [t[0] for t in token.tolist()][1:] == [100, 0, 7, 5, vocab - 1]
+    assert torch.equal(x, embed[token])
+    # row stride larger than the vocabulary (a view of a wider buffer), no embedding
+    wide = torch.randn((rows, vocab + 64), device="cuda", generator=g).to(dtype)
+    tok2 = torch.full((rows,), -1, dtype=torch.long, device="cuda")
+    _lib.check(_lib.lib().pf_argmax_embed(wide.data_ptr(), vocab + 64, vocab, rows, tok2.data_ptr(), None, None,
+                                          0, _lib.dtype_code(dtype), _lib.stream_of(wide)))
+    assert tok2.tolist() == torch.argmax(wide[:, :vocab], dim=-1).tolist()

@@ -375,6 +375,17 @@ int pf_silu_mul(const void* gate, const void* up, void* out, int dtype, long row
                      "pf_silu_mul");
 }
 
+int pf_argmax_embed(const void* logits, long row_stride, int vocab, int rows, int64_t* token, const void* embed,
+                    void* x, int dim, int dtype, void* stream) {
+  if (!valid_dtype(dtype) || !logits || !token || (embed && !x))
+    return fail(PF_ERR_INVALID, "pf_argmax_embed: bad argument");
+  if (rows < 0 || vocab <= 0 || row_stride < vocab || (embed && dim <= 0))
+    return fail(PF_ERR_INVALID, "pf_argmax_embed: bad shape");
+  return cuda_status(launch_argmax_embed(logits, row_stride, vocab, rows, token, embed, x, dim, dtype,
+                                         static_cast<cudaStream_t>(stream)),
+                     "pf_argmax_embed");
+}
+
 int pf_decode_positions(int64_t* pos, int capacity, int32_t* slots, int32_t* lens, int32_t* rope_rows, int B,
                         void* stream) {
   if (!pos || !slots || !lens || !rope_rows) return fail(PF_ERR_INVALID, "pf_decode_positions: bad argument");

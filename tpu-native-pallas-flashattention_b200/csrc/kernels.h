@@ -96,6 +96,8 @@ cudaError_t launch_add_rms_norm(const void* x, const void* res, const void* w, v
                                 long rows, int dim, float eps, cudaStream_t st);
 cudaError_t launch_silu_mul(const void* g, const void* u, void* out, int dtype, long rows, int cols, long in_stride,
                             cudaStream_t st);
+cudaError_t launch_argmax_embed(const void* logits, long row_stride, int vocab, int rows, int64_t* token,
+                                const void* embed, void* x, int dim, int dtype, cudaStream_t st);
 cudaError_t launch_decode_positions(int64_t* pos, int C, int32_t* slots, int32_t* lens, int32_t* rope_rows, int B,
                                     cudaStream_t st);
 cudaError_t launch_rope_apply(const void* x, const void* cos_t, const void* sin_t, int tdtype, void* out, int dtype,

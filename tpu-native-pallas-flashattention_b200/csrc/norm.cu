@@ -10,9 +10,11 @@
 // Each rounding is to the tensor dtype, at the same points as the unfused
 // PyTorch expressions (a bf16 add rounds its fp32 sum; silu rounds before the
 // product), with fp32 arithmetic in between.  A third kernel advances a
-// CUDA-graph decode step's position on the device.  In a decode step these replace
+// CUDA-graph decode step's position on the device, and a fourth ends the
+// step: greedy token choice plus the next step's embedding row.  In a decode step these replace
 // ~8 launches per norm and 2 per activation: at batch 16 the step is a chain
 // of small launches, so the count sets the token rate.
+#include <climits>
 #include "common.cuh"
 #include "kernels.h"
 
@@ -144,6 +146,60 @@ void launch_norm_warp(const void* x, const void* res, const void* w, void* x_out
       static_cast<uint4*>(x_out), static_cast<uint4*>(h), rows, dim, eps);
 }
 
+// Greedy-decode tail, one CTA per row b: token[b] = argmax_v logits[b, v] --
+// the first index of the maximum, a NaN ranking above every number (the
+// torch.argmax / jnp.argmax rule) -- and, when embed is given, x[b, :] =
+// embed[token[b], :], the next decode step's input row.
+struct ArgBest {
+  float f;
+  int i;
+  bool nan;
+};
+__device__ __forceinline__ bool arg_beats(const ArgBest& a, const ArgBest& b) {
+  if (a.nan != b.nan) return a.nan;
+  if (!a.nan && a.f != b.f) return a.f > b.f;
+  return a.i < b.i;
+}
+constexpr int kArgThreads = 512;
+template <typename T>
+__global__ void __launch_bounds__(kArgThreads)
+argmax_embed_kernel(const T* __restrict__ logits, long row_stride, int vocab, int64_t* __restrict__ token,
+                    const T* __restrict__ embed, T* __restrict__ x, int dim) {
+  __shared__ ArgBest part[kArgThreads / 32];
+  __shared__ int winner;
+  const int b = blockIdx.x;
+  const T* row = logits + (long)b * row_stride;
+  ArgBest best{-INFINITY, INT_MAX, false};
+  for (int v = threadIdx.x; v < vocab; v += kArgThreads) {
+    const float f = to_f(row[v]);
+    const ArgBest c{f, v, f != f};
+    if (arg_beats(c, best)) best = c;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    ArgBest c;
+    c.f = __shfl_xor_sync(0xffffffffu, best.f, o);
+    c.i = __shfl_xor_sync(0xffffffffu, best.i, o);
+    c.nan = __shfl_xor_sync(0xffffffffu, (int)best.nan, o) != 0;
+    if (arg_beats(c, best)) best = c;
+  }
+  if (threadIdx.x % 32 == 0) part[threadIdx.x / 32] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    ArgBest w = part[0];
+    for (int k = 1; k < kArgThreads / 32; ++k)
+      if (arg_beats(part[k], w)) w = part[k];
+    const int t = w.i == INT_MAX ? 0 : w.i;  // vocab == 0 cannot reach here
+    token[b] = t;
+    winner = t;
+  }
+  __syncthreads();
+  if (embed != nullptr) {
+    const T* src = embed + (long)winner * dim;
+    for (int d = threadIdx.x; d < dim; d += kArgThreads) x[(long)b * dim + d] = src[d];
+  }
+}
+
 template <typename T>
 cudaError_t launch_norm_t(const void* x, const void* res, const void* w, void* x_out, void* h, long rows, int dim,
                           float eps, cudaStream_t st) {
@@ -199,6 +255,19 @@ cudaError_t launch_silu_mul(const void* g, const void* u, void* out, int dtype, 
     case PF_BF16: return launch_silu_t<__nv_bfloat16>(g, u, out, rows, cols, in_stride, st);
     default: return launch_silu_t<__half>(g, u, out, rows, cols, in_stride, st);
   }
+}
+
+cudaError_t launch_argmax_embed(const void* logits, long row_stride, int vocab, int rows, int64_t* token,
+                                const void* embed, void* x, int dim, int dtype, cudaStream_t st) {
+  if (rows == 0) return cudaSuccess;
+#define PF_AE(T)                                                                                              \
+  argmax_embed_kernel<T><<<rows, kArgThreads, 0, st>>>(static_cast<const T*>(logits), row_stride, vocab, token, \
+                                                       static_cast<const T*>(embed), static_cast<T*>(x), dim)
+  if (dtype == PF_F32) PF_AE(float);
+  else if (dtype == PF_BF16) PF_AE(__nv_bfloat16);
+  else PF_AE(__half);
+#undef PF_AE
+  return cudaGetLastError();
 }
 
 cudaError_t launch_decode_positions(int64_t* pos, int C, int32_t* slots, int32_t* lens, int32_t* rope_rows, int B,

@@ -364,6 +364,8 @@ class DecodeGraph:
         self.params, self.cache, self.cfg = params, cache, cfg
         self.C = cache[0]["k"].shape[2]
         self.token = torch.zeros((batch, 1), dtype=torch.long, device=device)
+        # the next step's input rows, written by the previous step's argmax + embedding kernel
+        self.x = torch.zeros((batch, 1, cfg.dim), dtype=params["embed"].dtype, device=device)
         self.pos = torch.zeros((1,), dtype=torch.long, device=device)
         self.table = torch.arange(batch, dtype=torch.int32, device=device).reshape(batch, 1)
         self.slots = torch.zeros((batch,), dtype=torch.int32, device=device)
@@ -382,7 +384,7 @@ class DecodeGraph:
         _lib.check(_lib.lib().pf_decode_positions(self.pos.data_ptr(), self.C, self.slots.data_ptr(),
                                                   self.lens.data_ptr(), self.rope_rows.data_ptr(),
                                                   self.slots.numel(), _lib.stream_of(self.pos)))
-        x = p["embed"][self.token]
+        x = self.x
         batch = x.shape[0]
         mlp = None
         for layer, lc in zip(p["layers"], self.cache):
@@ -395,7 +397,14 @@ class DecodeGraph:
                                 layer["ffn_norm"], cfg.rms_norm_eps)
             mlp = swiglu_mlp(h, layer["w_gate"], layer["w_up"], layer["w_down"])
         x, h = add_rms_norm(x, mlp, p["final_norm"], cfg.rms_norm_eps)
-        self.token.copy_(_argmax_last(h @ p["lm_head"]))
+        logits = (h @ p["lm_head"]).contiguous()
+        embed = p["embed"].contiguous()
+        if embed.dtype != logits.dtype:
+            raise ValueError("the embedding table and lm_head must share a dtype for the graph decode step")
+        # greedy token (first maximum, as torch.argmax) and the next step's embedding row
+        _lib.check(_lib.lib().pf_argmax_embed(logits.data_ptr(), logits.shape[-1], logits.shape[-1], batch,
+                                              self.token.data_ptr(), embed.data_ptr(), self.x.data_ptr(),
+                                              cfg.dim, _lib.dtype_code(logits.dtype), _lib.stream_of(logits)))
 
     def capture(self, token, pos: int, last_pos: int):
         """One eager warm-up step at ``pos`` (it writes cache slot ``pos`` with the values the
@@ -404,15 +413,18 @@ class DecodeGraph:
         side = torch.cuda.Stream(device=self.device)
         side.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(side):
-            self.token.copy_(token)
-            self.pos.fill_(pos)
+            self._reset(token, pos)
             self._step()
         torch.cuda.current_stream().wait_stream(side)
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph):
             self._step()
+        self._reset(token, pos)
+
+    def _reset(self, token, pos: int):
         self.token.copy_(token)
         self.pos.fill_(pos)
+        self.x.copy_(self.params["embed"][self.token])
 
     def replay(self):
         self.graph.replay()
