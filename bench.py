@@ -570,7 +570,7 @@ def main():
     e2e_serial_ms = e0.elapsed_time(e1) / e2e_steps
     e2e_pipelined(pf, host_in, host_out, dev, 2)  # warm the copy streams
     barrier()
-    e2e_ms = e2e_pipelined(pf, host_in, host_out, dev, max(2, min(args.steps, 8)))
+    e2e_ms = e2e_pipelined(pf, host_in, host_out, dev, max(2, min(args.steps, 16)))
     if world > 1:
         t = torch.tensor([e2e_ms, e2e_serial_ms], device=dev)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)

@@ -131,3 +131,36 @@ def test_argmax_embed_matches_torch_argmax_and_lookup(dtype):
     _lib.check(_lib.lib().pf_argmax_embed(wide.data_ptr(), vocab + 64, vocab, rows, tok2.data_ptr(), None, None,
                                           0, _lib.dtype_code(dtype), _lib.stream_of(wide)))
     assert tok2.tolist() == torch.argmax(wide[:, :vocab], dim=-1).tolist()
+
+
+def test_norm_and_swiglu_are_differentiable_like_the_unfused_expressions():
+    """Gradients through add_rms_norm / rms_norm / swiglu_mlp (kernel forward, closed-form
+    backward) match torch autograd of the unfused expressions (fp32, relative 1e-4)."""
+    from pallas_flash import model
+    g = torch.Generator(device="cuda").manual_seed(6)
+
+    def leaf(*shape, scale=1.0):
+        return (scale * torch.randn(shape, device="cuda", generator=g)).requires_grad_(True)
+
+    x, r, w = leaf(3, 5, 64), leaf(3, 5, 64), leaf(64)
+    wg, wu, wd = leaf(64, 96, scale=0.1), leaf(64, 96, scale=0.1), leaf(96, 64, scale=0.1)
+    cot_x, cot_h = torch.randn((3, 5, 64), device="cuda", generator=g), torch.randn((3, 5, 64), device="cuda",
+                                                                                  generator=g)
+
+    def run(fused):
+        for t in (x, r, w, wg, wu, wd):
+            t.grad = None
+        if fused:
+            xs, h = model.add_rms_norm(x, r, w, 1e-5)
+            out = model.swiglu_mlp(h, wg, wu, wd) + model.rms_norm(xs, w, 1e-5)
+        else:
+            xs = x + r
+            h = unfused_norm(xs, w, 1e-5)
+            out = (torch.nn.functional.silu(h @ wg) * (h @ wu)) @ wd + unfused_norm(xs, w, 1e-5)
+        ((xs * cot_x).sum() + (out * cot_h).sum()).backward()
+        return [t.grad.clone() for t in (x, r, w, wg, wu, wd)]
+
+    got, want = run(True), run(False)
+    for name, a, b in zip(("x", "residual", "weight", "w_gate", "w_up", "w_down"), got, want):
+        rel = float((a - b).abs().max() / b.abs().max())
+        assert rel < 1e-4, (name, rel)

@@ -38,8 +38,8 @@ Cache = list  # per-layer list of {"k": [b, n_kv, cache_size, d], "v": same}
 # --------------------------------------------------------------------------- #
 # Building blocks (model.py:34-74)
 # --------------------------------------------------------------------------- #
-def add_rms_norm(x: torch.Tensor, residual: Optional[torch.Tensor], weight: torch.Tensor,
-                 eps: float):
+def _add_rms_norm_kernel(x: torch.Tensor, residual: Optional[torch.Tensor], weight: torch.Tensor,
+                         eps: float):
     """``x' = x + residual`` (``x' = x`` when ``residual`` is None) and ``rms_norm(x')``, as
     ``(x', h)`` from one kernel launch (``pf_add_rms_norm``).  The sum is rounded to
     ``x.dtype`` as the unfused ``x + residual`` rounds it; the norm follows model.py:34-38
@@ -63,6 +63,43 @@ def add_rms_norm(x: torch.Tensor, residual: Optional[torch.Tensor], weight: torc
                                           _lib.dtype_code(x.dtype), xc.numel() // dim, dim, float(eps),
                                           _lib.stream_of(x)))
     return x_out, h
+
+
+def _needs_grad(*ts) -> bool:
+    return torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in ts)
+
+
+class _RmsNormFn(torch.autograd.Function):
+    """rms_norm with the kernel forward and the closed-form fp32 gradient:
+    with r = rsqrt(mean(x^2) + eps) and g = dh * w,
+    dx = r * g - x * r^3 * mean(g * x),  dw = sum over rows of dh * x * r."""
+
+    @staticmethod
+    def forward(ctx, x, weight, eps):
+        ctx.save_for_backward(x, weight)
+        ctx.eps = eps
+        return _add_rms_norm_kernel(x, None, weight, eps)[1]
+
+    @staticmethod
+    def backward(ctx, dh):
+        x, w = ctx.saved_tensors
+        xf, gf = x.float(), dh.float() * w.float()
+        r = torch.rsqrt(xf.square().mean(dim=-1, keepdim=True) + ctx.eps)
+        dx = r * gf - xf * r.pow(3) * (gf * xf).mean(dim=-1, keepdim=True)
+        dw = (dh.float() * xf * r).reshape(-1, x.shape[-1]).sum(dim=0)
+        return dx.to(x.dtype), dw.to(w.dtype), None
+
+
+def add_rms_norm(x: torch.Tensor, residual: Optional[torch.Tensor], weight: torch.Tensor,
+                 eps: float):
+    """``x' = x + residual`` (``x' = x`` when ``residual`` is None) and ``rms_norm(x')``, as
+    ``(x', h)``: one kernel launch (``pf_add_rms_norm``) for inference.  When a gradient is
+    needed, the sum is a differentiable tensor add and the norm runs the same kernel inside
+    an autograd function (closed-form backward)."""
+    if _needs_grad(x, residual, weight):
+        xs = x if residual is None else x + residual.to(x.dtype)
+        return xs, _RmsNormFn.apply(xs, weight.to(x.dtype), float(eps))
+    return _add_rms_norm_kernel(x, residual, weight, eps)
 
 
 def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
@@ -90,7 +127,7 @@ def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.T
     return x * cos[None, None] + _rotate_half(x) * sin[None, None]
 
 
-def silu_mul(gate: torch.Tensor, up: Optional[torch.Tensor] = None) -> torch.Tensor:
+def _silu_mul_kernel(gate: torch.Tensor, up: Optional[torch.Tensor] = None) -> torch.Tensor:
     """``silu(gate) * up`` in one launch (``pf_silu_mul``); silu is rounded to the tensor
     dtype before the product, as in the unfused expression.  With ``up`` None, ``gate``
     is one fused ``[..., 2F]`` projection whose halves are the gate and the up values."""
@@ -117,6 +154,37 @@ def silu_mul(gate: torch.Tensor, up: Optional[torch.Tensor] = None) -> torch.Ten
     return out
 
 
+class _SiluMulFn(torch.autograd.Function):
+    """silu(g) * u with the kernel forward; with s = sigmoid(g):
+    dg = dout * u * s * (1 + g * (1 - s)),  du = dout * g * s (fp32)."""
+
+    @staticmethod
+    def forward(ctx, g, u):
+        ctx.save_for_backward(g, u)
+        return _silu_mul_kernel(g, u)
+
+    @staticmethod
+    def backward(ctx, dout):
+        g, u = ctx.saved_tensors
+        gf, uf, df = g.float(), u.float(), dout.float()
+        sg = torch.sigmoid(gf)
+        dg = df * uf * sg * (1 + gf * (1 - sg))
+        du = df * gf * sg
+        return dg.to(g.dtype), du.to(u.dtype)
+
+
+def silu_mul(gate: torch.Tensor, up: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``silu(gate) * up`` (``pf_silu_mul``); with ``up`` None, ``gate`` is one fused
+    ``[..., 2F]`` projection whose halves are the gate and the up values.  Differentiable:
+    when a gradient is needed the kernel runs inside an autograd function."""
+    if _needs_grad(gate, up):
+        if up is None:
+            cols = gate.shape[-1] // 2
+            gate, up = gate[..., :cols], gate[..., cols:]
+        return _SiluMulFn.apply(gate, up)
+    return _silu_mul_kernel(gate, up)
+
+
 # Column-concatenated copies of weight matrices, so that projections sharing an
 # input run as one matmul.  An entry is used only while every source tensor is
 # alive (weak references) and unmodified (its version counter): the cache never
@@ -125,6 +193,8 @@ _FUSED: Dict[tuple, tuple] = {}
 
 
 def _fused_columns(*ws: torch.Tensor) -> torch.Tensor:
+    if _needs_grad(*ws):  # a differentiable concatenation, rebuilt per call
+        return torch.cat(ws, dim=1)
     key = tuple(id(w) for w in ws)
     hit = _FUSED.get(key)
     if hit is not None:
