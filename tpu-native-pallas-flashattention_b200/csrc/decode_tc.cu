@@ -75,17 +75,31 @@ __device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], 
   }
 }
 
-// Byte address of (row, column d) in a tile of 128-byte-swizzled 64-column boxes.
+// Byte offset of row `row`, 64-column box `box` in a tile whose rows arrive in
+// segments of SEG rows, each segment laid out [box][row][128 B].  SEG = 32 (a
+// whole tile) is the plain [box][32 rows] layout; a paged tile whose pages
+// are 16 (or 8) rows long and whose two D = 128 halves come in one copy per
+// page segment has SEG = 16 (8).  SEG is a multiple of 8, so every segment
+// starts on a 1024-byte swizzle atom and (row & 7) is the swizzle phase.
+template <int D, int SEG>
+__device__ __forceinline__ uint32_t row_off(int row, int box) {
+  return (row / SEG) * (D / 64 * SEG * 128) + box * (SEG * 128) + (row % SEG) * 128;
+}
+// Byte address of (row, column d) in such a tile (128-byte swizzle).
+template <int D, int SEG>
 __device__ __forceinline__ uint32_t swz(uint32_t base, int row, int d) {
   const int box = d >> 6, chunk = (d & 63) >> 3;
-  return base + box * (kTileKeys * 128) + row * 128 + ((chunk ^ (row & 7)) << 4);
+  return base + row_off<D, SEG>(row, box) + ((chunk ^ (row & 7)) << 4);
 }
 
 // grid = (num_splits, Hkv * head_chunks, B); block = kWarps * 32.
-template <typename T, int D>
+// SEG: the tile's shared-memory segment length (see row_off); paired = the
+// paged maps bring both D = 128 halves of a page segment in one copy (SEG is
+// then the segment length), else one copy per 64-column half.
+template <typename T, int D, int SEG>
 __global__ void __launch_bounds__(kWarps * 32)
 decode_tc_kernel(DecodeArgs a, const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
-                 int head_chunks, int seg_rows) {
+                 int head_chunks, int seg_rows, bool paired) {
   using Cfg = TcCfg<D>;
   constexpr int FMT = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
   constexpr int NB = D / 8;  // output n-blocks
@@ -192,10 +206,17 @@ decode_tc_kernel(DecodeArgs a, const __grid_constant__ CUtensorMap tm_k, const _
         }
       }
       const int row = (int)(((long)page * a.Hkv + hk) * a.page_size + pos % a.page_size);
+      if (paired) {  // both halves of the segment in one copy each for K and V
+        const uint32_t off = row_off<D, SEG>(sg * seg_rows, 0);
+        tma_load_3d(kdst + off, &tm_k, bar, 0, row, 0);
+        tma_load_3d(vdst + off, &tm_v, bar, 0, row, 0);
+        continue;
+      }
 #pragma unroll
       for (int c = 0; c < Cfg::kBoxes; ++c) {
-        tma_load_3d(kdst + c * Cfg::kBoxBytes + sg * seg_rows * 128, &tm_k, bar, c * 64, row, 0);
-        tma_load_3d(vdst + c * Cfg::kBoxBytes + sg * seg_rows * 128, &tm_v, bar, c * 64, row, 0);
+        const uint32_t off = row_off<D, SEG>(sg * seg_rows, c);
+        tma_load_3d(kdst + off, &tm_k, bar, c * 64, row, 0);
+        tma_load_3d(vdst + off, &tm_v, bar, c * 64, row, 0);
       }
     }
   };
@@ -223,8 +244,8 @@ decode_tc_kernel(DecodeArgs a, const __grid_constant__ CUtensorMap tm_k, const _
       for (int i = lane; i < rows * 8 * Cfg::kBoxes; i += 32) {
         const int r = nv + i / (8 * Cfg::kBoxes), rest = i % (8 * Cfg::kBoxes);
         const int box = rest / 8, ch = rest % 8;
-        uint4* pk = reinterpret_cast<uint4*>(kbuf + box * Cfg::kBoxBytes + r * 128 + ch * 16);
-        uint4* pv = reinterpret_cast<uint4*>(vbuf + box * Cfg::kBoxBytes + r * 128 + ch * 16);
+        uint4* pk = reinterpret_cast<uint4*>(kbuf + row_off<D, SEG>(r, box) + ch * 16);
+        uint4* pv = reinterpret_cast<uint4*>(vbuf + row_off<D, SEG>(r, box) + ch * 16);
         *pk = make_uint4(0, 0, 0, 0);
         *pv = make_uint4(0, 0, 0, 0);
       }
@@ -245,7 +266,7 @@ decode_tc_kernel(DecodeArgs a, const __grid_constant__ CUtensorMap tm_k, const _
         uint32_t b0, b1, b2, b3;
         const int key = nb2 * 16 + (mi >> 1) * 8 + mr;
         const int d = ks * 16 + (mi & 1) * 8;
-        ldsm_x4(swz(kb, key, d), b0, b1, b2, b3);
+        ldsm_x4(swz<D, SEG>(kb, key, d), b0, b1, b2, b3);
         mma16816<FMT>(s[2 * nb2], qa[ks], b0, b1);
         mma16816<FMT>(s[2 * nb2 + 1], qa[ks], b2, b3);
       }
@@ -302,7 +323,7 @@ decode_tc_kernel(DecodeArgs a, const __grid_constant__ CUtensorMap tm_k, const _
         uint32_t b0, b1, b2, b3;
         const int key = ks * 16 + (mi & 1) * 8 + mr;
         const int d = nd2 * 16 + (mi >> 1) * 8;
-        ldsm_x4_t(swz(vb, key, d), b0, b1, b2, b3);
+        ldsm_x4_t(swz<D, SEG>(vb, key, d), b0, b1, b2, b3);
         mma16816<FMT>(o[2 * nd2], pa[ks], b0, b1);
         mma16816<FMT>(o[2 * nd2 + 1], pa[ks], b2, b3);
       }
@@ -364,11 +385,25 @@ decode_tc_kernel(DecodeArgs a, const __grid_constant__ CUtensorMap tm_k, const _
   }
 }
 
+template <typename T, int D, int SEG>
+cudaError_t launch_tc_kernel(const DecodeArgs& a, const CUtensorMap& tk, const CUtensorMap& tv, int seg_rows,
+                             bool paired) {
+  using Cfg = TcCfg<D>;
+  const int G = a.H / a.Hkv;
+  const int head_chunks = (G + 15) / 16;
+  auto kern = decode_tc_kernel<T, D, SEG>;
+  cudaError_t e = ensure_smem(kern, Cfg::kSmem);
+  if (e != cudaSuccess) return e;
+  dim3 grid(a.num_splits, a.Hkv * head_chunks, a.B);
+  kern<<<grid, kWarps * 32, Cfg::kSmem, a.stream>>>(a, tk, tv, head_chunks, seg_rows, paired);
+  return cudaGetLastError();
+}
+
 template <typename T, int D>
 cudaError_t launch_tc_t(const DecodeArgs& a) {
-  using Cfg = TcCfg<D>;
   CUtensorMap tk, tv;
   int seg_rows = kTileKeys;
+  bool paired = false;
   if (a.block_tables == nullptr) {
     if (!make_tile_map(&tk, a.k_src, a.dtype, D, a.fixed_len, a.cache_rows, a.B * a.Hkv, kTileKeys) ||
         !make_tile_map(&tv, a.v_src, a.dtype, D, a.fixed_len, a.cache_rows, a.B * a.Hkv, kTileKeys))
@@ -376,18 +411,18 @@ cudaError_t launch_tc_t(const DecodeArgs& a) {
   } else {
     seg_rows = a.page_size < kTileKeys ? a.page_size : kTileKeys;
     const long rows = (long)a.num_pages * a.Hkv * a.page_size;
-    if (!make_tile_map(&tk, a.k_src, a.dtype, D, (int)rows, rows, 1, seg_rows) ||
-        !make_tile_map(&tv, a.v_src, a.dtype, D, (int)rows, rows, 1, seg_rows))
+    // D = 128: one copy per page segment for both column halves (half the
+    // copies of two 64-column boxes; the copy count bounds small-page decode).
+    paired = D == 128 && make_paged_pair_map(&tk, a.k_src, a.dtype, rows, seg_rows) &&
+             make_paged_pair_map(&tv, a.v_src, a.dtype, rows, seg_rows);
+    if (!paired && (!make_tile_map(&tk, a.k_src, a.dtype, D, (int)rows, rows, 1, seg_rows) ||
+                    !make_tile_map(&tv, a.v_src, a.dtype, D, (int)rows, rows, 1, seg_rows)))
       return cudaErrorInvalidValue;
   }
-  const int G = a.H / a.Hkv;
-  const int head_chunks = (G + 15) / 16;
-  auto kern = decode_tc_kernel<T, D>;
-  cudaError_t e = ensure_smem(kern, Cfg::kSmem);
-  if (e != cudaSuccess) return e;
-  dim3 grid(a.num_splits, a.Hkv * head_chunks, a.B);
-  kern<<<grid, kWarps * 32, Cfg::kSmem, a.stream>>>(a, tk, tv, head_chunks, seg_rows);
-  e = cudaGetLastError();
+  cudaError_t e;
+  if (paired && seg_rows == 8) e = launch_tc_kernel<T, D, 8>(a, tk, tv, seg_rows, true);
+  else if (paired && seg_rows == 16) e = launch_tc_kernel<T, D, 16>(a, tk, tv, seg_rows, true);
+  else e = launch_tc_kernel<T, D, kTileKeys>(a, tk, tv, seg_rows, paired);
   if (e != cudaSuccess) return e;
   return launch_decode_combine(a);
 }

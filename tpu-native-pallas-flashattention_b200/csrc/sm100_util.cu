@@ -74,5 +74,22 @@ bool make_tile_map(CUtensorMap* m, const void* base, int dtype, int D, int rows,
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// A paged pool of D = 128 rows viewed so that one TMA box brings both 64-column
+// halves of `box_rows` consecutive rows: dims (64 columns, rows at 256 B, 2
+// halves at 128 B), box {64, box_rows, 2}; the box lands in shared memory as
+// [half][row][64 columns], the layout two {64, box_rows} boxes give.
+bool make_paged_pair_map(CUtensorMap* m, const void* base, int dtype, long rows, int box_rows) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (enc == nullptr) return false;
+  const CUtensorMapDataType dt =
+      dtype == PF_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  cuuint64_t dims[3] = {64, (cuuint64_t)rows, 2};
+  cuuint64_t strides[2] = {256, 128};
+  cuuint32_t box[3] = {64, (cuuint32_t)box_rows, 2};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return enc(m, dt, 3, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
 
 }  // namespace pf

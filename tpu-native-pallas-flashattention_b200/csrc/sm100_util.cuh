@@ -59,5 +59,8 @@ __device__ __forceinline__ uint32_t split_packed_col(int kk) {
 // box = 64 columns x box_rows rows, 128-byte swizzle, zero fill past `rows`.
 bool make_tile_map(CUtensorMap* m, const void* base, int dtype, int D, int rows,
                    long row_stride_rows, int planes, int box_rows);
+// A D = 128 paged pool as (64 columns, rows, 2 halves): one box of
+// {64, box_rows, 2} brings both column halves of box_rows rows.
+bool make_paged_pair_map(CUtensorMap* m, const void* base, int dtype, long rows, int box_rows);
 
 }  // namespace pf
