@@ -20,15 +20,24 @@ It restates, in numpy, the algorithm of the reference
 * ``ring_slots`` -- src/pallas_flash/model.py:434-449, :475-476;
 * ``TinyLlama`` -- src/pallas_flash/model.py:34-176 (forward only).
 
-Parity pinning: JAX is not installed here or on the GPU hosts, so the reference
-cannot be executed and stores no golden vectors (its tests draw inputs from
-jax.random at run time).  The oracle is pinned instead by (a) the reference's
-own known-answer tests (uniform attention over all-ones K/V returns exactly
-1.0, NaN beyond the valid length never leaks, shared pages give identical
-rows, key-order invariance, ring_kv_len values), and (b) the committed
-fixtures in tests/golden/, produced by tests/golden/make_golden.py with an
-independent float64 torch autograd of the same math.  Bit-level rounding of
-the TPU kernels is not reproduced (parity for floating point is by tolerance).
+Parity pinning: JAX is not installed here or on the GPU hosts, but the
+reference's own source runs under a numpy stand-in for the jax names it uses
+(tests/golden/jax_numpy_shim.py; ``pallas_call`` executes each Pallas kernel
+body grid point by grid point, as interpret mode does).
+tests/golden/make_reference_golden.py executes the UNMODIFIED reference files
+-- the forward/backward/decode/fused-RoPE/paged Pallas kernels, the naive
+``reference_attention``, the page helpers and the model's ``forward`` /
+``generate`` / ``generate_cached`` / ``generate_streaming`` -- with float32
+widened to float64, and stores their outputs in
+tests/golden/reference_golden.npz.  tests/test_reference_golden.py checks this
+oracle against those outputs (float32 rounding), and
+tests/test_reference_golden_gpu.py checks the CUDA kernels against them.
+Further pins: the reference tests' known-answer cases (uniform attention over
+all-ones K/V returns exactly 1.0, NaN beyond the valid length never leaks,
+shared pages give identical rows, key-order invariance, ring_kv_len values)
+and tests/golden/attention_cases.npz (float64 torch autograd of the same math,
+tests/golden/make_golden.py).  Bit-level rounding of the TPU kernels is not
+reproduced (parity for floating point is by tolerance).
 """
 
 from __future__ import annotations

@@ -16,7 +16,7 @@ import pytest
 
 ROOT = Path(__file__).resolve().parents[1]
 PKG = ROOT / "tpu-native-pallas-flashattention_b200"
-for p in (str(PKG), str(ROOT)):
+for p in (str(PKG), str(ROOT), str(ROOT / "tests" / "golden")):
     if p not in sys.path:
         sys.path.insert(0, p)
 
@@ -76,3 +76,16 @@ def widen(t):
 def rel_err(a, b):
     """max|a-b| / max|b| -- the reference's gradient metric (tests/test_backward.py:25-26)."""
     return float(np.max(np.abs(a - b)) / (np.max(np.abs(b)) + 1e-9))
+
+
+@pytest.fixture(scope="session")
+def ref_golden():
+    """Outputs of the reference's own source (tests/golden/make_reference_golden.py).
+
+    Keys are ``group/case/field``; inputs are rebuilt with ``golden_inputs``."""
+    data = np.load(ROOT / "tests" / "golden" / "reference_golden.npz")
+    return {k: data[k] for k in data.files}
+
+
+def bf16_bits_to_f32(bits):
+    return (np.asarray(bits, np.uint16).astype(np.uint32) << 16).view(np.float32)
