@@ -69,7 +69,9 @@ enum pf_status {
 enum pf_device_bits {
   PF_DEV_WAIT_TIMEOUT = 1, /* a bounded mbarrier wait gave up                     */
   PF_DEV_BAD_PAGE = 2,     /* a block-table entry was outside [0, num_pages)      */
-  PF_DEV_SMEM_LAYOUT = 4   /* dynamic shared memory was not 1024-byte aligned     */
+  PF_DEV_SMEM_LAYOUT = 4,  /* dynamic shared memory was not 1024-byte aligned     */
+  PF_DEV_LEN_OVER_MAX = 8  /* a context length exceeded the call's max_context_len:
+                              keys past the planned splits were not attended     */
 };
 
 const char* pf_last_error(void);
@@ -78,6 +80,16 @@ const char* pf_version(void);
 /* Reads the device status word of the current device (synchronises the
  * device); clears it when reset != 0. */
 int pf_device_status(int* bits_out, int reset);
+/* Sets the wall-time bound of every bounded in-kernel wait (mbarrier phases
+ * of the TMA/tcgen05 pipelines), in ns, on the current device; 0 restores the
+ * 2 s default.  A wait that runs out records PF_DEV_WAIT_TIMEOUT and its
+ * kernel returns.  No counterpart in the reference (its Pallas kernels have no
+ * device-side waits); provided so the timeout path can be tested. */
+int pf_set_wait_limit_ns(unsigned long long ns);
+/* Launches one CTA that waits on an mbarrier nothing arrives on: after the
+ * wait limit it records PF_DEV_WAIT_TIMEOUT and returns.  A self-test of the
+ * timeout path (no counterpart in the reference). */
+int pf_selftest_wait_timeout(void* stream);
 /* Which forward kernel family pf_fwd would use for these arguments:
  * 1 = tcgen05/TMEM tensor-core kernel, 0 = fp32 SIMT kernel. */
 int pf_fwd_kernel_kind(int dtype, int head_dim);

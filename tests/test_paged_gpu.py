@@ -88,6 +88,25 @@ def test_bad_page_id_is_flagged_not_faulted(dtype):
     assert _lib.device_status(reset=True) & _lib.PF_DEV_BAD_PAGE
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_length_above_max_context_len_is_flagged_or_rejected(dtype):
+    """A length beyond max_context_len is never silently truncated: device lengths
+    raise PF_DEV_LEN_OVER_MAX in the status word, host lengths raise ValueError."""
+    kp, vp = randn((64, 2, 16, 128), 4), randn((64, 2, 16, 128), 5)
+    q = randn((2, 4, 1, 128), 6)
+    table = torch.arange(64, dtype=torch.int32).reshape(2, 32)
+    args = (to_dev(q, dtype), to_dev(kp, dtype), to_dev(vp, dtype), table.cuda())
+    _lib.device_status(reset=True)
+    pf.paged_flash_attention(*args, torch.tensor([100, 300], dtype=torch.int32, device="cuda"),
+                             max_context_len=300)
+    assert _lib.device_status(reset=True) == 0
+    pf.paged_flash_attention(*args, torch.tensor([100, 500], dtype=torch.int32, device="cuda"),
+                             max_context_len=300)
+    assert _lib.device_status(reset=True) & _lib.PF_DEV_LEN_OVER_MAX
+    with pytest.raises(ValueError):
+        pf.paged_flash_attention(*args, torch.tensor([100, 500], dtype=torch.int32), max_context_len=300)
+
+
 @pytest.mark.parametrize("page_size", [8, 12, 48, 256])
 @pytest.mark.parametrize("D", [64, 128])
 def test_page_sizes_bf16(page_size, D):
@@ -369,3 +388,25 @@ def test_paged_prefill_single_token_equals_paged_decode():
     a = pf.paged_prefill_attention(q, kp, vp, tables, ctx)
     b = pf.paged_flash_attention(q, kp, vp, tables, ctx)
     assert float((a.float() - b.float()).abs().max()) < 2e-2
+
+
+def test_bounded_wait_times_out_with_a_status_not_a_hang():
+    """A wait on an mbarrier nothing arrives on gives up after the (test-shortened)
+    limit, records PF_DEV_WAIT_TIMEOUT and the kernel returns; the context stays
+    usable for the next call."""
+    L = _lib.lib()
+    _lib.device_status(reset=True)
+    assert L.pf_set_wait_limit_ns(2_000_000) == _lib.PF_OK  # 2 ms
+    try:
+        assert L.pf_selftest_wait_timeout(torch.cuda.current_stream().cuda_stream) == _lib.PF_OK
+        torch.cuda.synchronize()
+        assert _lib.device_status(reset=True) & _lib.PF_DEV_WAIT_TIMEOUT
+    finally:
+        assert L.pf_set_wait_limit_ns(0) == _lib.PF_OK
+    # the device still works, and ordinary calls raise no flag
+    kp, vp = randn((4, 2, 16, 64), 1), randn((4, 2, 16, 64), 2)
+    out = pf.paged_flash_attention(to_dev(randn((1, 4, 1, 64), 3), torch.bfloat16), to_dev(kp, torch.bfloat16),
+                                   to_dev(vp, torch.bfloat16), torch.tensor([[1, 2]], dtype=torch.int32),
+                                   torch.tensor([20], dtype=torch.int32))
+    assert torch.isfinite(out.float()).all()
+    assert _lib.device_status(reset=True) == 0

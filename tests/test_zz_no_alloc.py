@@ -58,9 +58,40 @@ def test_noalloc_matches_workspace_entry_point_twice(B, H, Hkv, ps, D, lens):
     max_len = table.shape[1] * ps
     want = pf.paged_flash_attention(q, kp, vp, table, ll, max_context_len=max_len)
     for call in range(2):
+        _lib.device_status(reset=True)
         st, got = _noalloc(q, kp, vp, table, ll, max_len)
         assert st == _lib.PF_OK, _lib.lib().pf_last_error().decode()
         torch.cuda.synchronize()
+        assert _lib.device_status(reset=True) == 0, call
+        err = float((got.float() - want.float()).abs().max())
+        assert err < BF16_TOL, (call, err)
+
+
+def test_noalloc_widened_splits_match_workspace_entry_point():
+    """At B=256, H=32, D=128 one split of partials is 4.26 MB, so the 16 MiB scratch
+    holds 3 splits where the workspace entry point plans 8: the no-alloc call widens
+    the splits to 11008 keys (beyond the 4096-key split that keeps a CTA's page ids
+    in shared memory).  Every table entry points into a small shared pool, so the
+    memory stays small while some sequences are longer than one widened split."""
+    B, H, Hkv, ps, D, pps = 256, 32, 8, 16, 128, 2048
+    g = torch.Generator(device="cuda").manual_seed(7)
+    num_pages = 97
+    kp = torch.randn((num_pages, Hkv, ps, D), device="cuda", generator=g).to(torch.bfloat16)
+    vp = torch.randn((num_pages, Hkv, ps, D), device="cuda", generator=g).to(torch.bfloat16)
+    q = torch.randn((B, H, 1, D), device="cuda", generator=g).to(torch.bfloat16)
+    table = torch.randint(0, num_pages, (B, pps), generator=torch.Generator().manual_seed(7),
+                          dtype=torch.int32).cuda()
+    lens = [17 + 13 * i for i in range(B)]
+    lens[3], lens[100], lens[200], lens[255] = 11009, 22050, 32768, 30000
+    ll = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    max_len = pps * ps
+    want = pf.paged_flash_attention(q, kp, vp, table, ll, max_context_len=max_len)
+    for call in range(2):
+        _lib.device_status(reset=True)
+        st, got = _noalloc(q, kp, vp, table, ll, max_len)
+        assert st == _lib.PF_OK, _lib.lib().pf_last_error().decode()
+        torch.cuda.synchronize()
+        assert _lib.device_status(reset=True) == 0, call
         err = float((got.float() - want.float()).abs().max())
         assert err < BF16_TOL, (call, err)
 
@@ -70,8 +101,11 @@ def test_noalloc_second_call_with_smaller_batch_ignores_stale_scratch():
     small = _case(2, 8, 2, 16, 128, [50, 300], seed=2)
     for q, kp, vp, table, ll in (big, small):
         max_len = table.shape[1] * 16
+        _lib.device_status(reset=True)
         st, got = _noalloc(q, kp, vp, table, ll, max_len)
         assert st == _lib.PF_OK
+        torch.cuda.synchronize()
+        assert _lib.device_status(reset=True) == 0
         want = pf.paged_flash_attention(q, kp, vp, table, ll, max_context_len=max_len)
         assert float((got.float() - want.float()).abs().max()) < BF16_TOL
 

@@ -450,7 +450,7 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
             umma_commit(&bars->pv_done);
             umma_commit(&bars->vempty[it % NS]);
             need_v2 = false;
-          } else if ((spin & 1023u) == 0 && global_timer_ns() - t0 > kWaitLimitNs) {
+          } else if ((spin & 1023u) == 0 && global_timer_ns() - t0 > *(volatile unsigned long long*)&g_wait_limit_ns) {
             flag_status(PF_DEV_WAIT_TIMEOUT);
             ok = false;
           }

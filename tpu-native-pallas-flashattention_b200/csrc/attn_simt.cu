@@ -18,6 +18,7 @@
 namespace pf {
 
 __device__ int g_status = 0;
+__device__ unsigned long long g_wait_limit_ns = kWaitLimitNs;
 #ifdef PF_TRACE
 __device__ unsigned long long g_trace[kTraceCtas * kTraceEvents];
 __device__ unsigned int g_trace_n[kTraceCtas];

@@ -4,6 +4,7 @@
 // flash_attention.py:527-545, fused_rope.py:154-181, paged.py:129-149),
 // picks the kernel family and launches on the caller's stream.  Nothing here
 // allocates device memory; scratch comes from the caller's workspace.
+#include <climits>
 #include <cstdio>
 #include <cstring>
 #include <cstdarg>
@@ -62,6 +63,20 @@ int set_last_error(int code, const char* fmt, ...) {
   va_end(ap);
   return code;
 }
+// One CTA waits (bounded) on an mbarrier that nothing ever arrives on: the
+// wait gives up after g_wait_limit_ns, records PF_DEV_WAIT_TIMEOUT and the
+// kernel returns.  Exercises the timeout path that every pipelined kernel
+// relies on, without any other kernel misbehaving.
+__global__ void wait_timeout_selftest_kernel() {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_wait(&bar, 0);
+  __syncthreads();
+}
 }  // namespace pf
 
 extern "C" {
@@ -82,6 +97,16 @@ int pf_device_status(int* bits_out, int reset) {
     if (e != cudaSuccess) return cuda_status(e, "pf_device_status");
   }
   return PF_OK;
+}
+
+int pf_set_wait_limit_ns(unsigned long long ns) {
+  const unsigned long long v = ns == 0 ? (unsigned long long)kWaitLimitNs : ns;
+  return cuda_status(cudaMemcpyToSymbol(g_wait_limit_ns, &v, sizeof(v)), "pf_set_wait_limit_ns");
+}
+
+int pf_selftest_wait_timeout(void* stream) {
+  wait_timeout_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>();
+  return cuda_status(cudaGetLastError(), "pf_selftest_wait_timeout");
 }
 
 #ifdef PF_TRACE
@@ -294,8 +319,10 @@ int pf_paged_decode(const void* q, const void* k_pages, const void* v_pages,
     return fail(PF_ERR_UNSUPPORTED, "pf_paged_decode: head_dim %d not built (64, 128, 256)", D);
   if (!aligned16(k_pages) || !aligned16(v_pages))
     return fail(PF_ERR_INVALID, "pf_paged_decode: page pools must be 16-byte aligned");
-  if (max_context_len <= 0) max_context_len = pages_per_seq * page_size;
-  max_context_len = max_context_len < pages_per_seq * page_size ? max_context_len : pages_per_seq * page_size;
+  const long long cap = (long long)pages_per_seq * page_size;
+  if (cap > INT_MAX)
+    return fail(PF_ERR_INVALID, "pf_paged_decode: pages_per_seq * page_size = %lld exceeds INT_MAX", cap);
+  if (max_context_len <= 0 || max_context_len > cap) max_context_len = (int)cap;
   DecodeArgs a{};
   a.q = q; a.k_src = k_pages; a.v_src = v_pages; a.block_tables = block_tables;
   a.context_lens = context_lens; a.o = o; a.dtype = dtype; a.B = B; a.H = H; a.Hkv = Hkv; a.D = D;

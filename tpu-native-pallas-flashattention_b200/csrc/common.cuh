@@ -46,6 +46,9 @@ constexpr float kLn2 = 0.6931471805599453f;
 // ---------------------------------------------------------------------------
 extern __device__ int g_status;
 __device__ __forceinline__ void flag_status(int bits) { atomicOr(&g_status, bits); }
+// Wall-time bound of every mbarrier wait, in ns (2 s unless pf_set_wait_limit_ns
+// changed it; read only once a wait has missed its first poll).
+extern __device__ unsigned long long g_wait_limit_ns;
 
 // Optional phase tracing for kernel development (compiled in only with
 // -DPF_TRACE): the first kTraceCtas CTAs store clock64() into fixed slots
@@ -108,13 +111,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Waits for the phase with the given parity to complete.  Gives up after
 // kWaitLimitNs of wall time, records PF_DEV_WAIT_TIMEOUT and returns false so
 // the caller can leave its loop instead of hanging the GPU.
-constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s default of g_wait_limit_ns
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
+  const uint64_t limit = *(volatile unsigned long long*)&g_wait_limit_ns;
   for (uint32_t it = 0;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 255u) == 255u && global_timer_ns() - t0 > kWaitLimitNs) {
+    if ((it & 255u) == 255u && global_timer_ns() - t0 > limit) {
       flag_status(PF_DEV_WAIT_TIMEOUT);
       return false;
     }
@@ -138,9 +142,10 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
 __device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity) {
   if (mbar_test(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
+  const uint64_t limit = *(volatile unsigned long long*)&g_wait_limit_ns;
   for (uint32_t it = 0;; ++it) {
     if (mbar_test(bar, parity)) return true;
-    if ((it & 1023u) == 1023u && global_timer_ns() - t0 > kWaitLimitNs) {
+    if ((it & 1023u) == 1023u && global_timer_ns() - t0 > limit) {
       flag_status(PF_DEV_WAIT_TIMEOUT);
       return false;
     }

@@ -13,12 +13,16 @@
 // Host code never hands the array's name to a kernel (in host code it is only
 // a stand-in symbol, not a device address).  The first call on each device
 // resolves the real address with cudaGetSymbolAddress while that device is
-// current, checks the result and caches it; that first call should come
-// before any stream capture.  All calls share the one array and nothing in it
+// current, checks the result and caches it for the life of the process; that
+// first call should come before any stream capture.  A cudaDeviceReset (or any
+// other teardown of the primary context) reloads the module and can move the
+// array, so a process that resets a device must not call this entry point
+// again on that device.  All calls share the one array and nothing in it
 // needs clearing (every partial the combine step reads is written earlier in
 // the same call), but calls that overlap on the GPU -- e.g. on two streams of
 // one device -- race on it.  Requests whose partials cannot fit even with a
 // single split per sequence are rejected with PF_ERR_WORKSPACE.
+#include <climits>
 #include <mutex>
 
 #include "common.cuh"
@@ -77,8 +81,10 @@ extern "C" int pf_paged_decode_noalloc(const void* q, const void* k_pages, const
     return set_last_error(PF_ERR_UNSUPPORTED, "%s: head_dim %d not built (64, 128, 256)", fn, D);
   if ((reinterpret_cast<uintptr_t>(k_pages) & 15u) || (reinterpret_cast<uintptr_t>(v_pages) & 15u))
     return set_last_error(PF_ERR_INVALID, "%s: page pools must be 16-byte aligned", fn);
-  const int cap = pages_per_seq * page_size;
-  if (max_context_len <= 0 || max_context_len > cap) max_context_len = cap;
+  const long long cap = (long long)pages_per_seq * page_size;
+  if (cap > INT_MAX)
+    return set_last_error(PF_ERR_INVALID, "%s: pages_per_seq * page_size = %lld exceeds INT_MAX", fn, cap);
+  if (max_context_len <= 0 || max_context_len > cap) max_context_len = (int)cap;
 
   // One split per sequence needs B*H*(D+2) floats; use more splits only while they fit.
   const size_t per_split = (size_t)B * H * (D + 2) * sizeof(float);

@@ -123,6 +123,10 @@ decode_tc_kernel(DecodeArgs a, const __grid_constant__ CUtensorMap tm_k, const _
     if (threadIdx.x == 0) flag_status(PF_DEV_BAD_PAGE);
     len = a.pages_per_seq * a.page_size;
   }
+  // A length beyond the call's promised maximum would lose the keys past the
+  // planned splits: record it (once per sequence and head group) instead of
+  // silently attending a prefix.
+  if (len > a.max_len && split == 0 && threadIdx.x == 0) flag_status(PF_DEV_LEN_OVER_MAX);
   const int k_begin = split * a.split_len;
   const int k_end = min(len, k_begin + a.split_len);
   if (k_begin >= k_end) return;  // uniform over the CTA

@@ -27,6 +27,7 @@ PF_ERR_WORKSPACE = 5
 PF_DEV_WAIT_TIMEOUT = 1
 PF_DEV_BAD_PAGE = 2
 PF_DEV_SMEM_LAYOUT = 4
+PF_DEV_LEN_OVER_MAX = 8
 
 _DTYPES = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
 
@@ -44,6 +45,8 @@ _SIGNATURES = {
     "pf_last_error": (ctypes.c_char_p, []),
     "pf_version": (ctypes.c_char_p, []),
     "pf_device_status": (_I, [ctypes.POINTER(_I), _I]),
+    "pf_set_wait_limit_ns": (_I, [ctypes.c_ulonglong]),
+    "pf_selftest_wait_timeout": (_I, [_P]),
     "pf_fwd_kernel_kind": (_I, [_I, _I]),
     "pf_fwd": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _F, _I, _P]),
     "pf_rope_fwd_workspace_size": (_Z, [_I, _I, _I, _I, _I]),

@@ -41,7 +41,10 @@ def paged_flash_attention(
 
     Returns ``[batch, num_heads, 1, head_dim]``.  ``max_context_len`` is an
     optional upper bound of ``context_lens`` (it sizes the split grid; the
-    default is the table capacity ``pages_per_seq * page_size``).
+    default is the table capacity ``pages_per_seq * page_size``).  A length
+    above it raises ``ValueError`` when ``context_lens`` is a host tensor; for
+    device lengths the kernel records ``PF_DEV_LEN_OVER_MAX`` in the device
+    status word (the keys past the planned splits are then not attended).
     """
     del interpret
     if q.ndim != 4 or q.shape[2] != 1:
@@ -75,6 +78,10 @@ def paged_flash_attention(
     pages_per_seq = tables.shape[1]
     cap = pages_per_seq * page_size
     max_len = cap if max_context_len is None else max(1, min(int(max_context_len), cap))
+    if max_context_len is not None and context_lens.device.type == "cpu" and context_lens.numel():
+        longest = int(context_lens.max())
+        if longest > max_len:
+            raise ValueError(f"context_lens has a length {longest} above max_context_len {max_len}")
     q, k_pages, v_pages = q.contiguous(), k_pages.contiguous(), v_pages.contiguous()
     out = torch.empty_like(q)
     L = _lib.lib()
