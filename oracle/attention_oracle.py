@@ -18,7 +18,9 @@ It restates, in numpy, the algorithm of the reference
 * ``gather_contiguous`` / ``paged_attention`` -- tests/test_paged.py:25-28 and
   the block-table index map of src/pallas_flash/paged.py:158-159;
 * ``ring_slots`` -- src/pallas_flash/model.py:434-449, :475-476;
-* ``TinyLlama`` -- src/pallas_flash/model.py:34-176 (forward only).
+* ``tiny_llama_forward`` -- src/pallas_flash/model.py:34-140;
+  ``tiny_llama_generate`` -- the fixed-cache and ring-cache greedy loops of
+  model.py:307-386 and :406-531.
 
 Parity pinning: JAX is not installed here or on the GPU hosts, but the
 reference's own source runs under a numpy stand-in for the jax names it uses
@@ -264,6 +266,65 @@ def tiny_llama_forward(params: dict, tokens: np.ndarray, cfg) -> np.ndarray:
         x = x + (_silu(h @ layer["w_gate"]) * (h @ layer["w_up"])) @ layer["w_down"]
     x = rms_norm(x, params["final_norm"], cfg.rms_norm_eps)
     return x @ params["lm_head"]
+
+
+def tiny_llama_generate(params: dict, prompts: np.ndarray, max_new_tokens: int, cfg,
+                        window: Optional[int] = None) -> np.ndarray:
+    """Greedy generation with a KV cache, numpy fp32.
+
+    ``window=None``: the fixed cache of ``generate_cached`` (model.py:307-386,
+    capacity prompt + new tokens); ``window=W``: the ring cache of
+    ``generate_streaming`` (model.py:406-531): the prompt is attended in full,
+    its last ``min(prompt, W)`` K/V rows are kept at slots ``pos % W``, and each
+    decode step writes slot ``pos % W`` and attends the ``min(pos + 1, W)``
+    live slots.  Returns ``[batch, prompt + max_new_tokens]`` token ids.
+    """
+    b, seq = prompts.shape
+    hd, nkv = cfg.head_dim, cfg.n_kv_heads
+    cap = seq + max_new_tokens if window is None else window
+    total = seq + max_new_tokens
+    cos_all, sin_all = precompute_rope(total, hd, cfg.rope_theta)
+
+    def split(t, n, length):
+        return t.reshape(b, length, n, hd).transpose(0, 2, 1, 3)
+
+    caches = [(np.zeros((b, nkv, cap, hd), np.float32), np.zeros((b, nkv, cap, hd), np.float32))
+              for _ in params["layers"]]
+    # prefill
+    x = params["embed"][prompts].astype(np.float32)
+    cos, sin = cos_all[:seq], sin_all[:seq]
+    keep = min(seq, cap)
+    slots = np.arange(seq - keep, seq) % cap
+    for layer, (kc, vc) in zip(params["layers"], caches):
+        h = rms_norm(x, layer["attn_norm"], cfg.rms_norm_eps)
+        q = apply_rope(split(h @ layer["wq"], cfg.n_heads, seq), cos, sin)
+        k = apply_rope(split(h @ layer["wk"], nkv, seq), cos, sin)
+        v = split(h @ layer["wv"], nkv, seq)
+        kc[:, :, slots] = k[:, :, seq - keep:]
+        vc[:, :, slots] = v[:, :, seq - keep:]
+        a = reference_attention(q, k, v, causal=True, dtype=np.float32)
+        x = x + a.transpose(0, 2, 1, 3).reshape(b, seq, cfg.dim) @ layer["wo"]
+        h = rms_norm(x, layer["ffn_norm"], cfg.rms_norm_eps)
+        x = x + (_silu(h @ layer["w_gate"]) * (h @ layer["w_up"])) @ layer["w_down"]
+    logits = rms_norm(x, params["final_norm"], cfg.rms_norm_eps)[:, -1] @ params["lm_head"]
+    out = [prompts, np.argmax(logits, axis=-1)[:, None]]
+    for i in range(max_new_tokens - 1):
+        pos = seq + i
+        slot, live = pos % cap, min(pos + 1, cap)
+        x = params["embed"][out[-1]].astype(np.float32)
+        cos, sin = cos_all[pos:pos + 1], sin_all[pos:pos + 1]
+        for layer, (kc, vc) in zip(params["layers"], caches):
+            h = rms_norm(x, layer["attn_norm"], cfg.rms_norm_eps)
+            q = apply_rope(split(h @ layer["wq"], cfg.n_heads, 1), cos, sin)
+            kc[:, :, slot] = apply_rope(split(h @ layer["wk"], nkv, 1), cos, sin)[:, :, 0]
+            vc[:, :, slot] = split(h @ layer["wv"], nkv, 1)[:, :, 0]
+            a = reference_attention(q, kc, vc, kv_len=live, dtype=np.float32)
+            x = x + a.transpose(0, 2, 1, 3).reshape(b, 1, cfg.dim) @ layer["wo"]
+            h = rms_norm(x, layer["ffn_norm"], cfg.rms_norm_eps)
+            x = x + (_silu(h @ layer["w_gate"]) * (h @ layer["w_up"])) @ layer["w_down"]
+        logits = rms_norm(x, params["final_norm"], cfg.rms_norm_eps)[:, -1] @ params["lm_head"]
+        out.append(np.argmax(logits, axis=-1)[:, None])
+    return np.concatenate(out, axis=1)
 
 
 # --------------------------------------------------------------------------- #

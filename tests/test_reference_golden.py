@@ -140,6 +140,12 @@ def test_oracle_model_matches_reference_logits_and_tokens(ref_golden, case):
         seq = np.concatenate([seq, nxt[:, None]], axis=1)
     np.testing.assert_array_equal(seq, ref_golden[f"model/{name}/tokens_cached"])
     assert float(ref_golden[f"model/{name}/margin_min"][0]) > 5e-3
+    # the oracle's cached and ring-cache loops give the reference's generate_cached /
+    # generate_streaming tokens
+    np.testing.assert_array_equal(orc.tiny_llama_generate(params, pr, n_new, cfg),
+                                  ref_golden[f"model/{name}/tokens_cached"])
+    np.testing.assert_array_equal(orc.tiny_llama_generate(params, pr, n_new, cfg, window=window),
+                                  ref_golden[f"model/{name}/tokens_stream"])
 
 
 def test_reference_ring_kv_len(ref_golden):
