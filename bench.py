@@ -62,7 +62,7 @@ FWD_FLOP = 4.0 * B * H * S * S * D / 2
 BWD_FLOP = 2.5 * FWD_FLOP
 STEP_FLOP = FWD_FLOP + BWD_FLOP
 UNITS = B * HKV  # independent (batch, kv-head group) units of the step
-LAUNCHES_PER_STEP = 4  # forward, delta preprocess, dQ, dK/dV
+LAUNCHES_PER_STEP = 4  # forward, delta preprocess, dK/dV (+ dS spill), dQ GEMM
 
 
 def peaks():
@@ -215,6 +215,37 @@ def time_kernels(pf, q, k, v, do, iters=5):
         fwd_ms += e[0].elapsed_time(e[1])
         bwd_ms += e[1].elapsed_time(e[2])
     return fwd_ms / iters, bwd_ms / iters
+
+
+def time_bwd_recompute(pf, q, k, v, do, iters=5):
+    """Device ms of the backward without the dS spill (workspace holding only delta: the dQ
+    kernel recomputes S and dP), for the record beside the default path."""
+    from pallas_flash import _lib
+    from pallas_flash.flash_attention import _fwd
+
+    b, h, sq, d = q.shape
+    hkv, sk = k.shape[1], k.shape[2]
+    scale = 1.0 / math.sqrt(d)
+    out, lse = _fwd(q, k, v, True, scale, sk, True)
+    L = _lib.lib()
+    ws = torch.empty(b * h * sq * 4, dtype=torch.uint8, device=q.device)
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+
+    def run():
+        _lib.check(L.pf_bwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), do.data_ptr(), lse.data_ptr(),
+                            dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), _lib.dtype_code(q.dtype), b, h, hkv, sq, sk,
+                            d, 1, scale, sk, ws.data_ptr(), ws.numel(), _lib.stream_of(q)))
+
+    run()
+    torch.cuda.synchronize()
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(iters):
+        run()
+    e1.record(s)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / iters
 
 
 # --------------------------------------------------------------------------- partitioning
@@ -812,8 +843,9 @@ def main():
 
     share = len(units) / UNITS
     fwd_ms, bwd_ms = time_kernels(pf, q, k, v, do)
+    bwd_recompute_ms = time_bwd_recompute(pf, q, k, v, do)
     hbm, tf_burst, tf_sust, src = peaks()
-    dom = (("backward (delta + dQ + dK/dV)", bwd_ms, BWD_FLOP * share) if bwd_ms >= fwd_ms
+    dom = (("backward (delta + dK/dV with dS spill + dQ GEMM)", bwd_ms, BWD_FLOP * share) if bwd_ms >= fwd_ms
            else ("forward", fwd_ms, FWD_FLOP * share))
     achieved = dom[2] / (dom[1] * 1e-3) / 1e12
     traffic = None
@@ -831,6 +863,7 @@ def main():
                      "traffic": traffic, "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
                      "fwd_tflops": FWD_FLOP * share / fwd_ms / 1e9, "bwd_tflops": BWD_FLOP * share / bwd_ms / 1e9,
                      "fwd_frac": FWD_FLOP * share / fwd_ms / 1e9 / tf_burst,
+                     "bwd_ms_without_ds_spill": bwd_recompute_ms,
                      "per_rank": "rank 0's kernels on its share of the units" if world > 1 else "whole problem"},
         "e2e": {"value": STEP_FLOP / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,

@@ -139,9 +139,14 @@ int pf_bwd_dkv(const void* q, const void* k, const void* v, const void* dout,
                int causal, float sm_scale, int kv_len, void* stream);
 
 /* Whole backward (preprocess + dQ + dK/dV) in one call.  The workspace holds
- * delta and, for the tensor-core path, an f32 dQ accumulator. */
+ * delta (B*H*Sq f32) and, on the tensor-core path, the dS spill: every 16-bit
+ * 128 x 128 dS tile the dK/dV kernel computes, from which dQ is one GEMM per
+ * query tile instead of a kernel that recomputes S and dP.
+ * pf_bwd_workspace_size returns the size with the spill (for these causal /
+ * kv_len arguments; kv_len <= 0 means Sk); pf_bwd accepts any workspace of at
+ * least the delta size and recomputes when the spill does not fit. */
 size_t pf_bwd_workspace_size(int dtype, int B, int H, int Hkv, int Sq, int Sk,
-                             int D);
+                             int D, int causal, int kv_len);
 int pf_bwd(const void* q, const void* k, const void* v, const void* o,
            const void* dout, const float* lse, void* dq, void* dk, void* dv,
            int dtype, int B, int H, int Hkv, int Sq, int Sk, int D,

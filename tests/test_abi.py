@@ -73,7 +73,12 @@ def test_workspace_queries_and_missing_workspace():
     assert lib.pf_paged_decode_workspace_size(256, 32, 8, 16, 32768, 128) == n
     st = lib.pf_decode(256, 256, 256, 256, 1, 1, 2, 2, 64, 128, 10, 0.1, None, 0, None)
     assert st == _lib.PF_ERR_WORKSPACE
-    assert lib.pf_bwd_workspace_size(1, 4, 32, 8, 4096, 4096, 128) >= 4 * 32 * 4096 * 4
+    # delta + the causal dS spill: 528 of the 32 x 32 tile pairs per plane, 32 KiB each
+    assert lib.pf_bwd_workspace_size(1, 4, 32, 8, 4096, 4096, 128, 1, 4096) == \
+        4 * 32 * 4096 * 4 + 4 * 32 * 528 * 32768
+    assert lib.pf_bwd_workspace_size(1, 4, 32, 8, 4096, 4096, 128, 0, 0) == \
+        4 * 32 * 4096 * 4 + 4 * 32 * 1024 * 32768
+    assert lib.pf_bwd_workspace_size(0, 4, 32, 8, 4096, 4096, 128, 1, 4096) == 4 * 32 * 4096 * 4  # fp32: no spill
 
 
 def test_paged_decode_validation():

@@ -22,6 +22,7 @@
 // (needs dP) -- with P kept in f32 registers between them, and the MMA issue
 // order interleaves the two kernels' GEMMs so that each phase overlaps tensor
 // work of a neighbouring tile.
+#include <climits>
 #include <type_traits>
 #include "common.cuh"
 #include "kernels.h"
@@ -73,6 +74,14 @@ struct BwdBars {
 };
 static_assert(sizeof(BwdBars) <= 256, "barrier block exceeds its shared-memory slot");
 
+// dK/dV with the dS spill: each elementwise warpgroup stages its 64-column
+// half of dS^T in the P^T tile once dV has read P^T, and one of its threads
+// sends it out with a TMA store.
+struct SpillBars {
+  uint64_t ds_written[2];  // the warpgroup's 128 threads wrote their dS^T rows
+  uint64_t ptile_free[2];  // the warpgroup's previous store finished reading the tile
+};
+
 // dK/dV: K, V resident; NS stages of (Q, dO) 128-row tiles plus their column statistics.
 template <int D>
 struct DkvCfg {
@@ -84,9 +93,10 @@ struct DkvCfg {
   static constexpr int kStatOff = kStreamOff + kNS * 2 * kTile;  // [kNS][2][128] f32: -lse*log2e, -delta
   static constexpr int kPOff = kStatOff + kNS * 256 * 4;   // P^T: 128 keys x 128 queries, SW128 K-major
   static constexpr int kBarOff = kPOff + 128 * 128 * 2;
+  static constexpr int kSpillBarOff = kBarOff + 256;
   // No alignment slack: at D = 128 the tiles fill the 227 KB limit, so the
   // kernel requires (and checks) a 1024-byte aligned dynamic shared window.
-  static constexpr int kSmem = kBarOff + 256;
+  static constexpr int kSmem = kSpillBarOff + 64;
   static_assert(kPOff % 1024 == 0, "P^T tile must be 1024-byte aligned");
   static constexpr uint32_t kS = 0, kDP = 128, kDV = 256, kDK = 256 + D;
 };
@@ -137,8 +147,7 @@ __device__ __forceinline__ void p_chunk_keep16(const uint32_t (&rs)[32], uint32_
 
 template <int FMT, typename ND>
 __device__ __forceinline__ void ds_chunk_keep16(const uint32_t (&rd)[32], const uint32_t (&keep)[16], ND nd,
-                                                uint32_t out) {
-  uint32_t pk[16];
+                                                uint32_t out, uint32_t (&pk)[16]) {
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
     const int c = 2 * i;
@@ -148,6 +157,21 @@ __device__ __forceinline__ void ds_chunk_keep16(const uint32_t (&rd)[32], const 
     pk[i] = FMT == 1 ? pack_bf16x2(ds.x, ds.y) : pack_f16x2(ds.x, ds.y);
   }
   tmem_st16(out, pk);
+}
+
+// dS spill layout: one 128 x 128 16-bit tile per live (key tile kt, query tile
+// qi) pair of a (batch, head) plane, rows = keys, columns = queries (row-major,
+// 256 B per row).  A plane's tiles are ordered by key tile, then query tile;
+// key tile kt has the query tiles [i0(kt), nq) with i0 = kt under the causal
+// mask (0 otherwise) and none when its first key is at or past kv_len.
+__host__ __device__ __forceinline__ long ds_tile_offset(int kt, int nq, int causal) {
+  // sum over k < kt of (nq - (causal ? min(k, nq) : 0))
+  long off = (long)kt * nq;
+  if (causal) off -= kt <= nq ? (long)kt * (kt - 1) / 2 : (long)nq * (nq - 1) / 2 + (long)(kt - nq) * nq;
+  return off;
+}
+__host__ __device__ __forceinline__ long ds_tiles_per_plane(int nq, int kv_len, int causal) {
+  return ds_tile_offset((kv_len + 127) / 128, nq, causal);
 }
 
 template <int FMT, bool FULL, typename NL2, typename Vis>
@@ -243,13 +267,18 @@ __device__ __forceinline__ void store_acc_row(uint32_t taddr, T* dst, int n, flo
 // ============================================================================
 // dK / dV
 // ============================================================================
-template <typename T, int D>
+// PT: P stays in TMEM (packed over the consumed S tile) and dV is a TS MMA;
+// the shared-memory tile then only stages the dS spill.  Otherwise P^T goes
+// through that tile and dV is an SS MMA, which lets S(it+1) be issued as soon
+// as S(it) is in registers.
+template <typename T, int D, bool PT>
 __global__ void __launch_bounds__(EwDkv::kThreads, 1)
 bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                      const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
+                     const __grid_constant__ CUtensorMap tm_ds, int spill,
                      const float* __restrict__ lse, const float* __restrict__ delta,
-                     T* __restrict__ dk, T* __restrict__ dv, int H, int Hkv, int Sq, int Sk,
-                     int kv_len, int causal, float sm_scale, float scale_log2, int n_kt) {
+                     T* __restrict__ dk, T* __restrict__ dv, int H, int Hkv,
+                     int Sq, int Sk, int kv_len, int causal, float sm_scale, float scale_log2, int n_kt) {
   using Cfg = DkvCfg<D>;
   constexpr int NS = Cfg::kNS;
   constexpr int kEWG = EwDkv::kEWG, kNCH = EwDkv::kNCH, kEWThreads = EwDkv::kEWThreads;
@@ -265,6 +294,7 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
   }
   uint8_t* smem = smem_raw;
   BwdBars* bars = reinterpret_cast<BwdBars*>(smem + Cfg::kBarOff);
+  SpillBars* sp = reinterpret_cast<SpillBars*>(smem + Cfg::kSpillBarOff);
   const uint32_t sbase = smem_u32(smem);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
 
@@ -298,6 +328,10 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
     mbar_init(&bars->ds_half, kEWThreads);
     mbar_init(&bars->s_free, kEWThreads + 1);  // + certifier: Q(it+1) and its statistics landed
     mbar_init(&bars->done, 1);
+    for (int w = 0; w < 2; ++w) {
+      mbar_init(&sp->ds_written[w], 128);
+      mbar_init(&sp->ptile_free[w], 1);
+    }
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -427,6 +461,31 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
         bool need_s = it + 1 < n_it, need_v1 = true, need_v2 = true;
         const uint64_t t0 = global_timer_ns();
         const uint64_t om = desc_mn_base<128>(do_addr);
+        if constexpr (PT) {
+          // dV(it) reads P from the S tile, so S(it+1) queues behind it.
+          ok = mbar_wait_spin(&bars->p_half, it & 1);
+          if (!ok) break;
+          tc_fence_after();
+          umma_ts(tmem + Cfg::kDV, tmem + Cfg::kS, om, idesc_acc, it > 0);
+          umma_ts_acc(tmem + Cfg::kDV, tmem + Cfg::kS + split_packed_col(1), om + mnoff(1), idesc_acc);
+          umma_ts_acc(tmem + Cfg::kDV, tmem + Cfg::kS + split_packed_col(4), om + mnoff(4), idesc_acc);
+          umma_ts_acc(tmem + Cfg::kDV, tmem + Cfg::kS + split_packed_col(5), om + mnoff(5), idesc_acc);
+          ok = mbar_wait_spin(&bars->p_ready, it & 1);
+          if (!ok) break;
+          tc_fence_after();
+          umma_ts_acc(tmem + Cfg::kDV, tmem + Cfg::kS + split_packed_col(2), om + mnoff(2), idesc_acc);
+          umma_ts_acc(tmem + Cfg::kDV, tmem + Cfg::kS + split_packed_col(3), om + mnoff(3), idesc_acc);
+          umma_ts_acc(tmem + Cfg::kDV, tmem + Cfg::kS + split_packed_col(6), om + mnoff(6), idesc_acc);
+          umma_ts_acc(tmem + Cfg::kDV, tmem + Cfg::kS + split_packed_col(7), om + mnoff(7), idesc_acc);
+          umma_commit(&bars->vempty[it % NS]);
+          if (need_s) {
+            ok = mbar_wait_spin(&bars->s_free, it & 1);  // Q(it+1) certified
+            if (!ok) break;
+            tc_fence_after();
+            issue_s(it + 1);
+          }
+          need_s = need_v2 = false;
+        }
         for (uint32_t spin = 1; ok && (need_s || need_v2); ++spin) {
           if (need_s && mbar_test(&bars->s_free, it & 1)) {  // Q(it+1) certified in the phase
             trace(14, it);
@@ -503,6 +562,7 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
     const int kpos = k0 + row;
     const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
     const bool key_ok = kpos < kv_len;
+    const bool spill_issuer = spill && warp == 2 + 4 * cw && lane == 0;  // sends the warpgroup's dS^T half
     const bool tr = lane == 0 && quad == 2 && cw < 2;  // trace writers
     const float2 sc2 = make_float2(scale_log2, scale_log2);
     bool ok = true;
@@ -541,16 +601,27 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
               return key_ok && qp < Sq && (!causal || qp >= kpos);
             });
           }
-          // The P^T tile is single-buffered: dV(it-1) must have read it.
-          if (h == 0 && it > 0 && !mbar_wait_spin(&bars->pv_done, (it - 1) & 1)) { ok = false; break; }
-          store_sw128_chunk(smem + Cfg::kPOff, row, col0 + 32 * h, pk[h]);
-          fence_proxy_async_smem();
-          if (h == 0) mbar_arrive(&bars->p_half);
+          if constexpr (PT) {
+            // P packed over the chunk's own (consumed) S columns: the A operand of dV.
+            tmem_st16(lane_base + Cfg::kS + col0 + 32 * h, pk[h]);
+            if (h == 0) {
+              tmem_wait_st();
+              tc_fence_before();
+              mbar_arrive(&bars->p_half);
+            }
+          } else {
+            // The P^T tile is single-buffered: dV(it-1) must have read it.
+            if (h == 0 && it > 0 && !mbar_wait_spin(&bars->pv_done, (it - 1) & 1)) { ok = false; break; }
+            store_sw128_chunk(smem + Cfg::kPOff, row, col0 + 32 * h, pk[h]);
+            fence_proxy_async_smem();
+            if (h == 0) mbar_arrive(&bars->p_half);
+          }
         }
         if (!ok) break;
         if (tr && cw == 0) trace(6, it);
       }
       if (tr && cw == 0) trace(7, it);
+      if constexpr (PT) tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&bars->p_ready);
       float nd[kNCH * 32];
@@ -560,22 +631,47 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
       tc_fence_after();
 #pragma unroll
       for (int h = 0; h < kNCH; ++h) {
-        uint32_t rd[32];
+        uint32_t rd[32], pkd[16];
         tmem_ld32(lane_base + Cfg::kDP + col0 + 32 * h, rd);
         tmem_wait_ld();
         ds_chunk_keep16<FMT>(rd, keep[h], [&](int c) { return make_float2(nd[32 * h + c], nd[32 * h + c + 1]); },
-                             lane_base + Cfg::kDP + col0 + 32 * h);
+                             lane_base + Cfg::kDP + col0 + 32 * h, pkd);
         if (h == 0) {  // first chunk of dS in place: dK may start on it
           tmem_wait_st();
           tc_fence_before();
           mbar_arrive(&bars->ds_half);
         }
+        if (spill) {  // dS^T rows into the staging tile once the previous store has read it
+          if (h == 0 && it > 0) {
+            if (spill_issuer) {
+              bulk_wait_read_all();
+              mbar_arrive(&sp->ptile_free[cw]);
+            }
+            if (!mbar_wait_spin(&sp->ptile_free[cw], (it - 1) & 1)) { ok = false; break; }
+          }
+          store_sw128_chunk(smem + Cfg::kPOff, row, col0 + 32 * h, pkd);
+        }
       }
+      if (!ok) break;
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&bars->ds_ready);
+      if (spill) {
+        fence_proxy_async_smem();
+        mbar_arrive(&sp->ds_written[cw]);
+        if (spill_issuer) {
+          if (!mbar_wait(&sp->ds_written[cw], it & 1)) { ok = false; break; }
+          const long plane = (long)b * H + hk * G + it / nqi;
+          const long tile = plane * ds_tiles_per_plane(nq, kv_len, causal) + ds_tile_offset(kt, nq, causal) +
+                            it % nqi;
+          tma_store_3d_hint(&tm_ds, smem + Cfg::kPOff + cw * (128 * 128), col0, 0, (int)tile,
+                            l2_evict_first_policy());
+          bulk_commit_group();
+        }
+      }
       if (tr) trace(10 + 3 * cw, it);
     }
+    if (spill_issuer) bulk_wait_all();  // the dS stores complete before the CTA exits
     // Epilogue: the first half of the warpgroups writes dV, the second half
     // dK (scaled), each a contiguous slice of the D columns.
     const bool have = n_it > 0 && ok && mbar_wait(&bars->done, 0);
@@ -840,24 +936,166 @@ bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
   }
 }
 
+// ============================================================================
+// dQ from the spilled dS tiles: dQ = scale * sum over key tiles of dS K
+// ============================================================================
+// The dK/dV kernel wrote every dS tile it computed (16-bit, rows = keys,
+// columns = queries); dQ of a 128-row query tile is then one GEMM over its key
+// tiles, A = dS (M = queries, K = keys, MN-major as stored) and B = K
+// (K = keys, N = D, MN-major), without recomputing S and dP.  It streams each
+// dS tile once from HBM, so it is bandwidth-bound (32 KB per tile pair
+// against 128 x 128 x D MACs).
+// Warp 0: TMA producer; warp 1: MMA issuer; warps 2-5: epilogue (a warp reads
+// TMEM lane quadrant warp % 4).
+template <int D>
+struct DqGemmCfg {
+  static constexpr int kNS = D == 128 ? 3 : 4;
+  static constexpr int kBoxes = D / 64;
+  static constexpr int kDsTile = 128 * 128 * 2;
+  static constexpr int kKTile = 128 * D * 2;
+  static constexpr int kStage = kDsTile + kKTile;
+  static constexpr int kBarOff = kNS * kStage;
+  static constexpr int kSmem = kBarOff + 256 + 1024;
+  static constexpr int kThreads = 6 * 32;
+  static constexpr uint32_t kCols = D;  // TMEM: the dQ accumulator
+};
+
+struct DqGemmBars {
+  uint64_t full[4], empty[4];
+  uint64_t done;
+  uint32_t tmem_base;
+};
+
 template <typename T, int D>
-cudaError_t launch_dkv_t(const BwdArgs& a) {
+__global__ void __launch_bounds__(DqGemmCfg<D>::kThreads, 1)
+bwd_dq_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tm_ds, const __grid_constant__ CUtensorMap tm_k,
+                         T* __restrict__ dq, int H, int Hkv, int Sq, int kv_len, int causal, float sm_scale,
+                         int n_qt) {
+  using Cfg = DqGemmCfg<D>;
+  constexpr int NS = Cfg::kNS;
+  constexpr int FMT = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
+  constexpr uint32_t idesc = make_idesc_f16(FMT, 128, D, 1, 1);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  DqGemmBars* bars = reinterpret_cast<DqGemmBars*>(smem + Cfg::kBarOff);
+  const uint32_t sbase = smem_u32(smem);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+
+  // Heaviest (last, under causal) query tiles first.
+  const int BH = gridDim.x / n_qt;
+  const int bh = blockIdx.x % BH;
+  const int qt = n_qt - 1 - blockIdx.x / BH;
+  const int b = bh / H, h = bh % H;
+  const int hk = h / (H / Hkv);
+  const int nkt = (kv_len + 127) / 128;
+  const int n_it = causal ? min(nkt, qt + 1) : nkt;
+  const long plane_tiles = ds_tiles_per_plane(n_qt, kv_len, causal);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->empty[s], 1);
+    }
+    mbar_init(&bars->done, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&bars->tmem_base, Cfg::kCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0 && n_it > 0) {
+      const uint64_t pol = l2_evict_first_policy();
+      int last = -1;
+      for (int it = 0; it < n_it; ++it) {
+        const int s = it % NS;
+        if (it >= NS && !mbar_wait(&bars->empty[s], ((it / NS) - 1) & 1)) break;
+        uint8_t* dst = smem + s * Cfg::kStage;
+        // tile of the pair (key tile it, query tile qt) in this plane
+        const long tile = (long)bh * plane_tiles + ds_tile_offset(it, n_qt, causal) + (qt - (causal ? it : 0));
+        mbar_expect_tx(&bars->full[s], Cfg::kStage);
+        for (int c = 0; c < 2; ++c)  // read once: evict first
+          tma_load_3d_hint(dst + c * 128 * 128, &tm_ds, &bars->full[s], c * 64, 0, (int)tile, pol);
+        for (int c = 0; c < Cfg::kBoxes; ++c)
+          tma_load_3d(dst + Cfg::kDsTile + c * 128 * 128, &tm_k, &bars->full[s], c * 64, it * 128, b * Hkv + hk);
+        last = it;
+      }
+      drain_ring(bars->full, NS, last);  // no copy may land after the CTA is gone
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && n_it > 0) {
+      bool ok = true;
+      for (int it = 0; ok && it < n_it; ++it) {
+        const int s = it % NS;
+        ok = mbar_wait_spin(&bars->full[s], (it / NS) & 1);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t ds_addr = sbase + s * Cfg::kStage;
+        const uint64_t ad = desc_mn_base<128>(ds_addr), bd = desc_mn_base<128>(ds_addr + Cfg::kDsTile);
+        umma_ss(tmem, ad, bd, idesc, it > 0);
+#pragma unroll
+        for (int kk = 1; kk < 8; ++kk) umma_ss_acc(tmem, ad + mnoff(kk), bd + mnoff(kk), idesc);
+        umma_commit(&bars->empty[s]);
+      }
+      umma_commit(&bars->done);
+    }
+  } else {
+    const int quad = warp % 4;
+    const int row = quad * 32 + lane;
+    const int qpos = qt * 128 + row;
+    const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
+    const bool have = n_it > 0 && mbar_wait(&bars->done, 0);
+    if (n_it > 0) tc_fence_after();
+    store_acc_row<T, FMT>(lane_base, dq + ((long)bh * Sq + qpos) * D, D, sm_scale, !have, qpos < Sq);
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    // `done` follows every MMA this CTA issued, so TMEM is never freed under a running MMA.
+    if (lane == 0 && n_it > 0) mbar_wait(&bars->done, 0);
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, Cfg::kCols);
+  }
+}
+
+template <typename T, int D, bool PT>
+cudaError_t launch_dkv_pt(const BwdArgs& a) {
   using Cfg = DkvCfg<D>;
-  CUtensorMap tk, tv, tq, tdo;
+  CUtensorMap tk, tv, tq, tdo, tds;
   const int BH = a.B * a.H, BHk = a.B * a.Hkv;
   if (!make_tile_map(&tk, a.k, a.dtype, D, a.kv_len, a.Sk, BHk, 128) ||
       !make_tile_map(&tv, a.v, a.dtype, D, a.kv_len, a.Sk, BHk, 128) ||
       !make_tile_map(&tq, a.q, a.dtype, D, a.Sq, a.Sq, BH, 128) ||
       !make_tile_map(&tdo, a.dout, a.dtype, D, a.Sq, a.Sq, BH, 128))
     return cudaErrorInvalidValue;
-  auto kern = bwd_dkv_sm100_kernel<T, D>;
+  const int spill = a.ds_buf != nullptr;
+  tds = tk;  // unused without the spill
+  if (spill) {
+    const long tiles = (long)BH * ds_tiles_per_plane((a.Sq + 127) / 128, a.kv_len, a.causal);
+    if (tiles <= 0 || tiles > INT_MAX || !make_tile_map(&tds, a.ds_buf, a.dtype, 128, 128, 128, (int)tiles, 128))
+      return cudaErrorInvalidValue;
+  }
+  auto kern = bwd_dkv_sm100_kernel<T, D, PT>;
   cudaError_t e = ensure_smem(kern, Cfg::kSmem);
   if (e != cudaSuccess) return e;
   const int n_kt = (a.Sk + 127) / 128;
-  kern<<<n_kt * BHk, EwDkv::kThreads, Cfg::kSmem, a.stream>>>(tk, tv, tq, tdo, a.lse, a.delta, (T*)a.dk, (T*)a.dv, a.H,
-                                                       a.Hkv, a.Sq, a.Sk, a.kv_len, a.causal, a.sm_scale,
-                                                       a.sm_scale * kLog2e, n_kt);
+  kern<<<n_kt * BHk, EwDkv::kThreads, Cfg::kSmem, a.stream>>>(tk, tv, tq, tdo, tds, spill, a.lse, a.delta,
+                                                       (T*)a.dk, (T*)a.dv, a.H, a.Hkv, a.Sq, a.Sk, a.kv_len,
+                                                       a.causal, a.sm_scale, a.sm_scale * kLog2e, n_kt);
   return cudaGetLastError();
+}
+
+template <typename T, int D>
+cudaError_t launch_dkv_t(const BwdArgs& a) {
+  return a.ds_buf != nullptr ? launch_dkv_pt<T, D, true>(a) : launch_dkv_pt<T, D, false>(a);
 }
 
 template <typename T, int D>
@@ -880,7 +1118,36 @@ cudaError_t launch_dq_t(const BwdArgs& a) {
   return cudaGetLastError();
 }
 
+template <typename T, int D>
+cudaError_t launch_dq_gemm_t(const BwdArgs& a) {
+  using Cfg = DqGemmCfg<D>;
+  const int BH = a.B * a.H, BHk = a.B * a.Hkv;
+  const int n_qt = (a.Sq + 127) / 128;
+  const long tiles = (long)BH * ds_tiles_per_plane(n_qt, a.kv_len, a.causal);
+  if (tiles <= 0 || tiles > INT_MAX) return cudaErrorInvalidValue;
+  CUtensorMap tds, tk;
+  if (!make_tile_map(&tds, a.ds_buf, a.dtype, 128, 128, 128, (int)tiles, 128) ||
+      !make_tile_map(&tk, a.k, a.dtype, D, a.kv_len, a.Sk, BHk, 128))
+    return cudaErrorInvalidValue;
+  auto kern = bwd_dq_gemm_sm100_kernel<T, D>;
+  cudaError_t e = ensure_smem(kern, Cfg::kSmem);
+  if (e != cudaSuccess) return e;
+  kern<<<n_qt * BH, Cfg::kThreads, Cfg::kSmem, a.stream>>>(tds, tk, (T*)a.dq, a.H, a.Hkv, a.Sq, a.kv_len, a.causal,
+                                                         a.sm_scale, n_qt);
+  return cudaGetLastError();
+}
+
 }  // namespace
+
+size_t bwd_ds_spill_bytes(int B, int H, int Sq, int kv_len, int causal) {
+  return (size_t)B * H * ds_tiles_per_plane((Sq + 127) / 128, kv_len, causal) * (128 * 128 * 2);
+}
+
+cudaError_t launch_bwd_dq_gemm_sm100(const BwdArgs& a) {
+  if (a.dtype == PF_BF16)
+    return a.D == 128 ? launch_dq_gemm_t<__nv_bfloat16, 128>(a) : launch_dq_gemm_t<__nv_bfloat16, 64>(a);
+  return a.D == 128 ? launch_dq_gemm_t<__half, 128>(a) : launch_dq_gemm_t<__half, 64>(a);
+}
 
 bool bwd_sm100_supported(int dtype, int D) { return fwd_sm100_supported(dtype, D); }
 

@@ -225,19 +225,29 @@ int pf_bwd_dkv(const void* q, const void* k, const void* v, const void* dout, co
   return cuda_status(launch_bwd_dkv_simt(a), "pf_bwd_dkv");
 }
 
-size_t pf_bwd_workspace_size(int dtype, int B, int H, int Hkv, int Sq, int Sk, int D) {
-  (void)dtype; (void)Hkv; (void)Sk; (void)D;
-  const size_t delta = ((size_t)B * H * Sq * sizeof(float) + 255) / 256 * 256;
-  return delta;
+static size_t bwd_delta_bytes(int B, int H, int Sq) {
+  return ((size_t)B * H * Sq * sizeof(float) + 255) / 256 * 256;
+}
+
+size_t pf_bwd_workspace_size(int dtype, int B, int H, int Hkv, int Sq, int Sk, int D, int causal,
+                             int kv_len) {
+  (void)Hkv;
+  if (B <= 0 || H <= 0 || Sq <= 0 || Sk <= 0) return 0;
+  const size_t delta = bwd_delta_bytes(B, H, Sq);
+  if (!bwd_sm100_supported(dtype, D)) return delta;
+  if (kv_len <= 0 || kv_len > Sk) kv_len = Sk;
+  return delta + bwd_ds_spill_bytes(B, H, Sq, kv_len, causal != 0);
 }
 
 int pf_bwd(const void* q, const void* k, const void* v, const void* o, const void* dout,
            const float* lse, void* dq, void* dk, void* dv, int dtype, int B, int H, int Hkv,
            int Sq, int Sk, int D, int causal, float sm_scale, int kv_len, void* workspace,
            size_t workspace_bytes, void* stream) {
-  const size_t need = pf_bwd_workspace_size(dtype, B, H, Hkv, Sq, Sk, D);
+  if (B <= 0 || H <= 0 || Sq <= 0) return fail(PF_ERR_INVALID, "pf_bwd: shapes must be positive");
+  const size_t need = bwd_delta_bytes(B, H, Sq);
   if (workspace == nullptr || workspace_bytes < need)
-    return fail(PF_ERR_WORKSPACE, "pf_bwd: workspace of %zu bytes required, got %zu", need, workspace_bytes);
+    return fail(PF_ERR_WORKSPACE, "pf_bwd: workspace of at least %zu bytes required, got %zu", need,
+                workspace_bytes);
   if (!o) return fail(PF_ERR_INVALID, "pf_bwd: null o");
   float* delta = static_cast<float*>(workspace);
   BwdArgs a;
@@ -249,6 +259,16 @@ int pf_bwd(const void* q, const void* k, const void* v, const void* o, const voi
   st = cuda_status(launch_bwd_preprocess(o, dout, delta, dtype, (long)B * H * Sq, D, a.stream), "pf_bwd (delta)");
   if (st != PF_OK) return st;
   if (use_tc_bwd(a)) {
+    // With room for the dS spill: dK/dV writes every dS tile and dQ is one GEMM
+    // over them (5 tile GEMMs per key/query tile pair); otherwise the dQ kernel
+    // recomputes S and dP (7).
+    const size_t spill = bwd_ds_spill_bytes(B, H, Sq, kv_len, a.causal);
+    if (workspace_bytes >= need + spill) {
+      a.ds_buf = reinterpret_cast<uint16_t*>(static_cast<uint8_t*>(workspace) + need);
+      st = cuda_status(launch_bwd_dkv_sm100(a), "pf_bwd (dkv + dS spill, tcgen05)");
+      if (st != PF_OK) return st;
+      return cuda_status(launch_bwd_dq_gemm_sm100(a), "pf_bwd (dq gemm, tcgen05)");
+    }
     st = cuda_status(launch_bwd_dkv_sm100(a), "pf_bwd (dkv, tcgen05)");
     if (st != PF_OK) return st;
     return cuda_status(launch_bwd_dq_sm100(a), "pf_bwd (dq, tcgen05)");

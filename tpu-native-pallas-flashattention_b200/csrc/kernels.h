@@ -34,6 +34,7 @@ struct BwdArgs {
   int dtype, B, H, Hkv, Sq, Sk, D, causal, kv_len;
   float sm_scale;
   float* dq_accum;  // f32 [B,H,Sq,D] scratch (tensor-core path)
+  uint16_t* ds_buf;  // dS spill of the dK/dV kernel for the dQ GEMM (null: not written)
   cudaStream_t stream;
 };
 
@@ -74,6 +75,10 @@ cudaError_t launch_rope_fwd_sm100(const FwdArgs& a, void* k_rot);
 // tcgen05 tensor-core backward (same dtypes / head dims as the forward).
 bool bwd_sm100_supported(int dtype, int D);
 cudaError_t launch_bwd_dkv_sm100(const BwdArgs& a);
+// Bytes of the dS spill (16-bit 128 x 128 tiles of every live key/query tile pair).
+size_t bwd_ds_spill_bytes(int B, int H, int Sq, int kv_len, int causal);
+// dQ as one GEMM over the spilled dS tiles (after launch_bwd_dkv_sm100 with ds_buf set).
+cudaError_t launch_bwd_dq_gemm_sm100(const BwdArgs& a);
 cudaError_t launch_bwd_dq_sm100(const BwdArgs& a);
 
 // Split-KV decode.

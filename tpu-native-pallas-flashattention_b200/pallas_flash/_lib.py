@@ -58,7 +58,7 @@ _SIGNATURES = {
     "pf_bwd_preprocess": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _P]),
     "pf_bwd_dq": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _F, _I, _P]),
     "pf_bwd_dkv": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _F, _I, _P]),
-    "pf_bwd_workspace_size": (_Z, [_I, _I, _I, _I, _I, _I, _I]),
+    "pf_bwd_workspace_size": (_Z, [_I, _I, _I, _I, _I, _I, _I, _I, _I]),
     "pf_bwd": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _F, _I, _P, _Z, _P]),
     "pf_decode_workspace_size": (_Z, [_I, _I, _I, _I, _I]),
     "pf_decode": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _F, _P, _Z, _P]),

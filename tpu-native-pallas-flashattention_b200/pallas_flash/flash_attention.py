@@ -86,7 +86,7 @@ def _bwd(q, k, v, out, lse, do, causal, sm_scale, kv_len):
     dv = torch.empty_like(v)
     L = _lib.lib()
     code = _lib.dtype_code(q.dtype)
-    ws_bytes = L.pf_bwd_workspace_size(code, B, H, Hkv, Sq, Sk, D)
+    ws_bytes = L.pf_bwd_workspace_size(code, B, H, Hkv, Sq, Sk, D, int(bool(causal)), int(kv_len))
     ws = _lib.workspace(ws_bytes, q.device)
     _lib.check(L.pf_bwd(
         q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), do.data_ptr(), lse.data_ptr(),
