@@ -692,8 +692,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-extras", action="store_true", help="skip the secondary workloads and CPU baselines")
-    ap.add_argument("--mode", choices=["bench", "profile-c2", "profile-decode", "profile-gen", "profile-rope",
-                                       "profile-fixed"], default="bench",
+    ap.add_argument("--mode", choices=["bench", "profile-c2", "profile-bwd", "profile-decode", "profile-decode-f32",
+                                       "profile-gen", "profile-rope", "profile-fixed"], default="bench",
                     help="profile-*: only launch the kernels of one workload (for ncu captures)")
     args = ap.parse_args()
 
@@ -738,6 +738,35 @@ def main():
     if args.mode == "profile-decode":
         # config-4 shape on 32 sequences (~2.4 GB of KV): warmup + steps decode calls
         paged_decode_bench(pf, dev, iters=args.steps, n_seqs=32, warmup=args.warmup)
+        print(json.dumps({"mode": args.mode, "ok": True}))
+        return
+    if args.mode == "profile-decode-f32":
+        # the config-4 shape on 8 sequences in fp32 (the bulk-copy split-KV kernel; ~1.2 GB of KV)
+        lens, npages, _, table = paged_problem(8)
+        pool = sum(npages)
+        g = torch.Generator(device=dev).manual_seed(0)
+        kp = torch.randn((pool, 8, 16, 128), device=dev, generator=g)
+        vp = torch.randn((pool, 8, 16, 128), device=dev, generator=g)
+        q = torch.randn((8, 32, 1, 128), device=dev, generator=g)
+        tt = torch.from_numpy(np.ascontiguousarray(table % pool)).to(dev)
+        ll = torch.from_numpy(lens.astype(np.int32)).to(dev)
+        for _ in range(args.warmup + args.steps):
+            pf.paged_flash_attention(q, kp, vp, tt, ll, max_context_len=32768)
+        torch.cuda.synchronize()
+        print(json.dumps({"mode": args.mode, "ok": True}))
+        return
+    if args.mode == "profile-bwd":
+        # one batch of config 2 (B1 H32 Hkv8 S4096 D128 causal): warmup + steps backward passes
+        from pallas_flash.flash_attention import _fwd, _bwd
+        g = torch.Generator(device=dev).manual_seed(0)
+        q = torch.randn((1, H, S, D), device=dev, generator=g).to(torch.bfloat16)
+        k = torch.randn((1, HKV, S, D), device=dev, generator=g).to(torch.bfloat16)
+        v = torch.randn((1, HKV, S, D), device=dev, generator=g).to(torch.bfloat16)
+        do = torch.randn((1, H, S, D), device=dev, generator=g).to(torch.bfloat16)
+        out, lse = _fwd(q, k, v, True, 1.0 / math.sqrt(D), S, True)
+        for _ in range(args.warmup + args.steps):
+            _bwd(q, k, v, out, lse, do, True, 1.0 / math.sqrt(D), S)
+        torch.cuda.synchronize()
         print(json.dumps({"mode": args.mode, "ok": True}))
         return
     if args.mode == "profile-fixed":

@@ -22,6 +22,7 @@
 // (needs dP) -- with P kept in f32 registers between them, and the MMA issue
 // order interleaves the two kernels' GEMMs so that each phase overlaps tensor
 // work of a neighbouring tile.
+#include <algorithm>
 #include <climits>
 #include <type_traits>
 #include "common.cuh"
@@ -945,6 +946,10 @@ bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
 // (K = keys, N = D, MN-major), without recomputing S and dP.  It streams each
 // dS tile once from HBM, so it is bandwidth-bound (32 KB per tile pair
 // against 128 x 128 x D MACs).
+// Persistent: one CTA per SM walks query-tile items (heaviest first, in
+// serpentine rounds), the producer streams (dS, K) stages across item
+// boundaries and the dQ accumulator is double-buffered in TMEM, so an item's
+// epilogue overlaps the next item's loads and MMAs.
 // Warp 0: TMA producer; warp 1: MMA issuer; warps 2-5: epilogue (a warp reads
 // TMEM lane quadrant warp % 4).
 template <int D>
@@ -957,20 +962,26 @@ struct DqGemmCfg {
   static constexpr int kBarOff = kNS * kStage;
   static constexpr int kSmem = kBarOff + 256 + 1024;
   static constexpr int kThreads = 6 * 32;
-  static constexpr uint32_t kCols = D;  // TMEM: the dQ accumulator
+  static constexpr uint32_t kCols = 2 * D;  // TMEM: two dQ accumulators
 };
 
 struct DqGemmBars {
   uint64_t full[4], empty[4];
+  uint64_t acc_full[2], acc_empty[2];
   uint64_t done;
   uint32_t tmem_base;
 };
+
+// The item a CTA processes in its round r (serpentine over the CTAs).
+__device__ __forceinline__ int dq_gemm_item(int r, int cta, int ctas) {
+  return r * ctas + ((r & 1) ? ctas - 1 - cta : cta);
+}
 
 template <typename T, int D>
 __global__ void __launch_bounds__(DqGemmCfg<D>::kThreads, 1)
 bwd_dq_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tm_ds, const __grid_constant__ CUtensorMap tm_k,
                          T* __restrict__ dq, int H, int Hkv, int Sq, int kv_len, int causal, float sm_scale,
-                         int n_qt) {
+                         int n_qt, int n_items) {
   using Cfg = DqGemmCfg<D>;
   constexpr int NS = Cfg::kNS;
   constexpr int FMT = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
@@ -982,20 +993,23 @@ bwd_dq_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tm_ds, const __grid
   const uint32_t sbase = smem_u32(smem);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
 
-  // Heaviest (last, under causal) query tiles first.
-  const int BH = gridDim.x / n_qt;
-  const int bh = blockIdx.x % BH;
-  const int qt = n_qt - 1 - blockIdx.x / BH;
-  const int b = bh / H, h = bh % H;
-  const int hk = h / (H / Hkv);
+  const int BH = n_items / n_qt;
   const int nkt = (kv_len + 127) / 128;
-  const int n_it = causal ? min(nkt, qt + 1) : nkt;
   const long plane_tiles = ds_tiles_per_plane(n_qt, kv_len, causal);
+  const int ctas = gridDim.x, cta = blockIdx.x;
+  const int n_rounds = (n_items + ctas - 1) / ctas;
+  // Item w: query tile qt = n_qt - 1 - w / BH (heaviest first under causal), plane bh = w % BH.
+  auto item_qt = [&](int w) { return n_qt - 1 - w / BH; };
+  auto item_iters = [&](int w) { return causal ? min(nkt, item_qt(w) + 1) : nkt; };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < NS; ++s) {
       mbar_init(&bars->full[s], 1);
       mbar_init(&bars->empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&bars->acc_full[a], 1);
+      mbar_init(&bars->acc_empty[a], 128);
     }
     mbar_init(&bars->done, 1);
     fence_barrier_init();
@@ -1010,56 +1024,84 @@ bwd_dq_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tm_ds, const __grid
   const uint32_t tmem = bars->tmem_base;
 
   if (warp == 0) {
-    if (lane == 0 && n_it > 0) {
+    if (lane == 0) {
       const uint64_t pol = l2_evict_first_policy();
-      int last = -1;
-      for (int it = 0; it < n_it; ++it) {
-        const int s = it % NS;
-        if (it >= NS && !mbar_wait(&bars->empty[s], ((it / NS) - 1) & 1)) break;
-        uint8_t* dst = smem + s * Cfg::kStage;
-        // tile of the pair (key tile it, query tile qt) in this plane
-        const long tile = (long)bh * plane_tiles + ds_tile_offset(it, n_qt, causal) + (qt - (causal ? it : 0));
-        mbar_expect_tx(&bars->full[s], Cfg::kStage);
-        for (int c = 0; c < 2; ++c)  // read once: evict first
-          tma_load_3d_hint(dst + c * 128 * 128, &tm_ds, &bars->full[s], c * 64, 0, (int)tile, pol);
-        for (int c = 0; c < Cfg::kBoxes; ++c)
-          tma_load_3d(dst + Cfg::kDsTile + c * 128 * 128, &tm_k, &bars->full[s], c * 64, it * 128, b * Hkv + hk);
-        last = it;
+      int g = 0, last = -1;  // stage counter across items
+      bool ok = true;
+      for (int r = 0; ok && r < n_rounds; ++r) {
+        const int w = dq_gemm_item(r, cta, ctas);
+        if (w >= n_items) continue;
+        const int qt = item_qt(w), bh = w % BH, n_it = item_iters(w);
+        const int kvp = (bh / H) * Hkv + (bh % H) / (H / Hkv);
+        for (int it = 0; it < n_it; ++it, ++g) {
+          const int s = g % NS;
+          if (g >= NS && !mbar_wait(&bars->empty[s], ((g / NS) - 1) & 1)) { ok = false; break; }
+          uint8_t* dst = smem + s * Cfg::kStage;
+          const long tile = (long)bh * plane_tiles + ds_tile_offset(it, n_qt, causal) + (qt - (causal ? it : 0));
+          mbar_expect_tx(&bars->full[s], Cfg::kStage);
+          for (int c = 0; c < 2; ++c)  // read once: evict first
+            tma_load_3d_hint(dst + c * 128 * 128, &tm_ds, &bars->full[s], c * 64, 0, (int)tile, pol);
+          for (int c = 0; c < Cfg::kBoxes; ++c)
+            tma_load_3d(dst + Cfg::kDsTile + c * 128 * 128, &tm_k, &bars->full[s], c * 64, it * 128, kvp);
+          last = g;
+        }
       }
       drain_ring(bars->full, NS, last);  // no copy may land after the CTA is gone
     }
   } else if (warp == 1) {
-    if (lane == 0 && n_it > 0) {
+    if (lane == 0) {
       bool ok = true;
-      for (int it = 0; ok && it < n_it; ++it) {
-        const int s = it % NS;
-        ok = mbar_wait_spin(&bars->full[s], (it / NS) & 1);
-        if (!ok) break;
+      int g = 0, j = 0;  // stage counter, item counter of this CTA
+      for (int r = 0; ok && r < n_rounds; ++r) {
+        const int w = dq_gemm_item(r, cta, ctas);
+        if (w >= n_items) continue;
+        const int n_it = item_iters(w);
+        const int ab = j & 1;
+        if (j >= 2 && !mbar_wait_spin(&bars->acc_empty[ab], ((j >> 1) - 1) & 1)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t ds_addr = sbase + s * Cfg::kStage;
-        const uint64_t ad = desc_mn_base<128>(ds_addr), bd = desc_mn_base<128>(ds_addr + Cfg::kDsTile);
-        umma_ss(tmem, ad, bd, idesc, it > 0);
+        const uint32_t acc = tmem + ab * D;
+        for (int it = 0; it < n_it; ++it, ++g) {
+          const int s = g % NS;
+          if (!mbar_wait_spin(&bars->full[s], (g / NS) & 1)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t ds_addr = sbase + s * Cfg::kStage;
+          const uint64_t ad = desc_mn_base<128>(ds_addr), bd = desc_mn_base<128>(ds_addr + Cfg::kDsTile);
+          umma_ss(acc, ad, bd, idesc, it > 0);
 #pragma unroll
-        for (int kk = 1; kk < 8; ++kk) umma_ss_acc(tmem, ad + mnoff(kk), bd + mnoff(kk), idesc);
-        umma_commit(&bars->empty[s]);
+          for (int kk = 1; kk < 8; ++kk) umma_ss_acc(acc, ad + mnoff(kk), bd + mnoff(kk), idesc);
+          umma_commit(&bars->empty[s]);
+        }
+        if (!ok) break;
+        umma_commit(&bars->acc_full[ab]);
+        ++j;
       }
       umma_commit(&bars->done);
     }
   } else {
     const int quad = warp % 4;
     const int row = quad * 32 + lane;
-    const int qpos = qt * 128 + row;
     const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
-    const bool have = n_it > 0 && mbar_wait(&bars->done, 0);
-    if (n_it > 0) tc_fence_after();
-    store_acc_row<T, FMT>(lane_base, dq + ((long)bh * Sq + qpos) * D, D, sm_scale, !have, qpos < Sq);
+    bool ok = true;
+    int j = 0;
+    for (int r = 0; r < n_rounds; ++r) {
+      const int w = dq_gemm_item(r, cta, ctas);
+      if (w >= n_items) continue;
+      const int qpos = item_qt(w) * 128 + row, bh = w % BH;
+      const int ab = j & 1;
+      if (ok) ok = mbar_wait(&bars->acc_full[ab], (j >> 1) & 1);
+      tc_fence_after();
+      store_acc_row<T, FMT>(lane_base + ab * D, dq + ((long)bh * Sq + qpos) * D, D, sm_scale, !ok, qpos < Sq);
+      tc_fence_before();
+      mbar_arrive(&bars->acc_empty[ab]);
+      ++j;
+    }
   }
 
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     // `done` follows every MMA this CTA issued, so TMEM is never freed under a running MMA.
-    if (lane == 0 && n_it > 0) mbar_wait(&bars->done, 0);
+    if (lane == 0) mbar_wait(&bars->done, 0);
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, Cfg::kCols);
@@ -1132,8 +1174,10 @@ cudaError_t launch_dq_gemm_t(const BwdArgs& a) {
   auto kern = bwd_dq_gemm_sm100_kernel<T, D>;
   cudaError_t e = ensure_smem(kern, Cfg::kSmem);
   if (e != cudaSuccess) return e;
-  kern<<<n_qt * BH, Cfg::kThreads, Cfg::kSmem, a.stream>>>(tds, tk, (T*)a.dq, a.H, a.Hkv, a.Sq, a.kv_len, a.causal,
-                                                         a.sm_scale, n_qt);
+  const int n_items = n_qt * BH;
+  const int grid = std::min(n_items, sm_count());
+  kern<<<grid, Cfg::kThreads, Cfg::kSmem, a.stream>>>(tds, tk, (T*)a.dq, a.H, a.Hkv, a.Sq, a.kv_len, a.causal,
+                                                    a.sm_scale, n_qt, n_items);
   return cudaGetLastError();
 }
 
