@@ -1,16 +1,22 @@
 // attn_bwd_sm100.cu -- tensor-core (tcgen05 / TMEM / TMA) backward for bf16
 // and f16 inputs, head_dim 64 or 128.
 //
-// Two kernels with transposed loops, as the reference's backward
-// (flash_attention.py:276-351), each recomputing P from the saved
-// log-sum-exp:  p = exp(s*scale - lse),  ds = p (dp - delta):
-//
+// The reference's backward (flash_attention.py:276-351) runs two kernels with
+// transposed loops, each recomputing P from the saved log-sum-exp:
+//   p = exp(s*scale - lse),  ds = p (dp - delta).
+// Here:
 //   dK/dV kernel: CTA = (batch, kv head, 128-key tile).  Loops over every q
 //     head of the GQA group and every 128-row query tile that can see the
 //     keys, so the group-sum of flash_attention.py:433-436 happens in TMEM:
 //        S^T  = K Q^T         dP^T = V dO^T            (M = 128 keys, N = 128)
 //        dV  += P^T dO        dK  += dS^T Q             (A = P^T, dS^T from TMEM)
-//   dQ kernel:    CTA = (batch, head, 128-row query tile), loops over 128-key tiles:
+//     With the dS spill (pf_bwd with room in its workspace) it also writes
+//     every 16-bit dS tile to global memory (TMA stores from a staging tile).
+//   dQ GEMM:      persistent; dQ of a 128-row query tile = scale * sum over its
+//     key tiles of dS K, streaming the spilled tiles (HBM-bound), so each
+//     (key tile, query tile) pair costs 5 tile GEMMs instead of 7.
+//   dQ kernel (without the spill): CTA = (batch, head, 128-row query tile),
+//     loops over 128-key tiles recomputing S and dP:
 //        S    = Q K^T         dP   = dO V^T             (M = 128 rows, N = 128)
 //        dQ  += dS K                                     (A = dS from TMEM)
 //
@@ -19,9 +25,8 @@
 // tiles reach only ~2/3 of it.  TMEM (512 columns) holds S and dP (128 each)
 // and the accumulators (dV, dK: 2 x D; dQ: D, with S double-buffered).  The
 // elementwise warps work in two phases per tile -- P (exp, needs S) then dS
-// (needs dP) -- with P kept in f32 registers between them, and the MMA issue
-// order interleaves the two kernels' GEMMs so that each phase overlaps tensor
-// work of a neighbouring tile.
+// (needs dP) -- and the MMA issue order interleaves the GEMMs so that each
+// phase overlaps tensor work of a neighbouring tile.
 #include <algorithm>
 #include <climits>
 #include <type_traits>
@@ -1137,7 +1142,9 @@ cudaError_t launch_dkv_pt(const BwdArgs& a) {
 
 template <typename T, int D>
 cudaError_t launch_dkv_t(const BwdArgs& a) {
-  return a.ds_buf != nullptr ? launch_dkv_pt<T, D, true>(a) : launch_dkv_pt<T, D, false>(a);
+  // P in TMEM (TS dV) measured faster with and without the spill (config 2,
+  // same box: 1017 vs 1099 us without it); the SS-dV variant stays for comparison.
+  return launch_dkv_pt<T, D, true>(a);
 }
 
 template <typename T, int D>
