@@ -30,6 +30,9 @@ constexpr int kBQ = 16;       // query rows per CTA (4 warps x 4 rows)
 constexpr int kBK = 32;       // keys per smem tile (one per lane)
 constexpr int kThreads = 128;
 constexpr int kRowsPerWarp = kBQ / (kThreads / 32);
+// Key groups per forward CTA (shared memory: one K and one V tile per group).
+template <int DMAX>
+constexpr int fwd_groups() { return DMAX == 256 ? 2 : 4; }
 
 // Loads rows [row0, row0 + nrows) of a [rows_total, D] matrix into smem
 // (stride ld floats), zero-filling rows past `valid` and columns past D.
@@ -56,9 +59,40 @@ __device__ void load_tile(float* dst, int ld, const T* src, int row0, int nrows,
   }
 }
 
-// Forward.  grid = (ceil(Sq / kBQ), H, B).
-template <typename T, int DMAX>
-__global__ void __launch_bounds__(kThreads)
+// Like load_tile, by the 128 threads of one key group (`tid` in [0, 128)).
+template <typename T>
+__device__ void load_tile_group(float* dst, int ld, const T* src, int row0, int nrows, int valid, int D, int DMAX,
+                                const void* cos_t, const void* sin_t, int tbl_dtype, int tid) {
+  const int half = D / 2;
+  for (int idx = tid; idx < nrows * DMAX; idx += 128) {
+    const int r = idx / DMAX, c = idx % DMAX;
+    const int row = row0 + r;
+    float x = 0.f;
+    if (row < valid && c < D) {
+      x = to_f(src[(long)row * D + c]);
+      if (cos_t != nullptr) {
+        const float partner = (c < half) ? -to_f(src[(long)row * D + c + half])
+                                         : to_f(src[(long)row * D + c - half]);
+        x = x * load_any(cos_t, tbl_dtype, (long)row * D + c) +
+            partner * load_any(sin_t, tbl_dtype, (long)row * D + c);
+      }
+    }
+    dst[r * ld + c] = x;
+  }
+}
+
+__device__ __forceinline__ void group_sync(int group) {  // the 128 threads of key group `group`
+  asm volatile("bar.sync %0, 128;" ::"r"(group + 1) : "memory");
+}
+
+// Forward.  grid = (ceil(Sq / kBQ), H, B); kFwdGroups key groups of 4 warps
+// per CTA split the key loop of the CTA's 16 query rows (every group takes
+// every kFwdGroups-th key tile) and merge their (max, sum, accumulator) at
+// the end, so the heaviest causal tile's serial chain is kFwdGroups times
+// shorter.  Each group's warps run the same loop (its barrier is the
+// group's own, the usual __syncthreads pattern within the group).
+template <typename T, int DMAX, int kFwdGroups = fwd_groups<DMAX>()>
+__global__ void __launch_bounds__(kThreads * kFwdGroups)
 fwd_simt_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
                 T* __restrict__ o, float* __restrict__ lse, int H, int Hkv, int Sq, int Sk,
                 int D, int causal, float sm_scale, int kv_len_max, const void* q_cos,
@@ -67,14 +101,16 @@ fwd_simt_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __res
   constexpr int LD = DMAX + 1;
   constexpr int NPL = DMAX / 32;  // output dims per lane
   extern __shared__ float smem[];
-  float* sQ = smem;                 // [kBQ][LD]
-  float* sK = sQ + kBQ * LD;        // [kBK][LD]
-  float* sV = sK + kBK * LD;        // [kBK][LD]
+  const int kg = threadIdx.x / kThreads;     // key group
+  const int gtid = threadIdx.x % kThreads;   // thread within the group
+  float* sQ = smem;                                          // [kBQ][LD]
+  float* sK = sQ + kBQ * LD + kg * 2 * kBK * LD;             // [kBK][LD] of this group
+  float* sV = sK + kBK * LD;                                 // [kBK][LD]
 
   // Heaviest (last, under causal) query tiles first: they set the tail.
   const int qb = gridDim.x - 1 - blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int hk = h / (H / Hkv);
-  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int warp = (threadIdx.x / 32) % (kThreads / 32), lane = threadIdx.x % 32;
   const int q0 = qb * kBQ;
   // Keys of this sequence and the position of query row 0 (causal offset).
   const int kv_len = kv_lens ? max(0, min(kv_lens[b], kv_len_max)) : kv_len_max;
@@ -84,6 +120,7 @@ fwd_simt_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __res
   const T* vp = v + ((long)b * Hkv + hk) * Sk * D;
 
   load_tile<T>(sQ, LD, qp, q0, kBQ, Sq, D, DMAX, q_cos, q_sin, tbl_dtype);
+  __syncthreads();
 
   float m[kRowsPerWarp], l[kRowsPerWarp], acc[kRowsPerWarp][NPL];
 #pragma unroll
@@ -97,11 +134,11 @@ fwd_simt_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __res
   // Last key any row of this tile may see (block skipping, :136-147).
   int k_end = kv_len;
   if (causal) k_end = min(k_end, q0 + q_off + kBQ);
-  for (int k0 = 0; k0 < k_end; k0 += kBK) {
-    __syncthreads();
-    load_tile<T>(sK, LD, kp, k0, kBK, kv_len, D, DMAX, k_cos, k_sin, tbl_dtype);
-    load_tile<T>(sV, LD, vp, k0, kBK, kv_len, D, DMAX, nullptr, nullptr, 0);
-    __syncthreads();
+  for (int k0 = kg * kBK; k0 < k_end; k0 += kFwdGroups * kBK) {
+    group_sync(kg);
+    load_tile_group<T>(sK, LD, kp, k0, kBK, kv_len, D, DMAX, k_cos, k_sin, tbl_dtype, gtid);
+    load_tile_group<T>(sV, LD, vp, k0, kBK, kv_len, D, DMAX, nullptr, nullptr, 0, gtid);
+    group_sync(kg);
     const int kpos = k0 + lane;
     // Scores of this lane's key for all of the warp's rows at once: the rows
     // are independent FMA chains (columns past D are zero in shared memory).
@@ -146,6 +183,49 @@ fwd_simt_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __res
         for (int i = 0; i < NPL; ++i) acc[r][i] = fmaf(pj, vj[i], acc[r][i]);
       }
     }
+  }
+
+  // Merge the key groups: group g's (m, l, acc) of row i go to shared memory
+  // (over the K/V tiles), then group 0 rescales to the common maximum.
+  __syncthreads();
+  float* mrg = smem + kBQ * LD;  // [kFwdGroups][kBQ][DMAX + 2]
+  constexpr int MS = DMAX + 2;
+#pragma unroll
+  for (int r = 0; r < kRowsPerWarp; ++r) {
+    float* slot = mrg + ((long)kg * kBQ + warp * kRowsPerWarp + r) * MS;
+#pragma unroll
+    for (int i = 0; i < NPL; ++i) slot[lane + 32 * i] = acc[r][i];
+    if (lane == 0) {
+      slot[DMAX] = m[r];
+      slot[DMAX + 1] = l[r];
+    }
+  }
+  __syncthreads();
+  if (kg != 0) return;
+#pragma unroll
+  for (int r = 0; r < kRowsPerWarp; ++r) {
+    const int row = warp * kRowsPerWarp + r;
+    float mx = -INFINITY;
+#pragma unroll
+    for (int g = 0; g < kFwdGroups; ++g) mx = fmaxf(mx, mrg[((long)g * kBQ + row) * MS + DMAX]);
+    float lsum = 0.f, a[NPL];
+#pragma unroll
+    for (int i = 0; i < NPL; ++i) a[i] = 0.f;
+    if (mx != -INFINITY) {
+#pragma unroll
+      for (int g = 0; g < kFwdGroups; ++g) {
+        const float* slot = mrg + ((long)g * kBQ + row) * MS;
+        const float gm = slot[DMAX];
+        const float w = gm == -INFINITY ? 0.f : expf(gm - mx);
+        lsum += slot[DMAX + 1] * w;
+#pragma unroll
+        for (int i = 0; i < NPL; ++i) a[i] = fmaf(slot[lane + 32 * i], w, a[i]);
+      }
+    }
+    m[r] = mx;
+    l[r] = lsum;
+#pragma unroll
+    for (int i = 0; i < NPL; ++i) acc[r][i] = a[i];
   }
 
 #pragma unroll
@@ -413,12 +493,15 @@ bwd_dkv_simt_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* _
 template <typename T, int DMAX>
 cudaError_t launch_fwd_t(const FwdArgs& a) {
   constexpr int LD = DMAX + 1;
-  const size_t smem = (size_t)(kBQ + 2 * kBK) * LD * sizeof(float);
+  constexpr int kFwdGroups = fwd_groups<DMAX>();
+  const size_t tiles = (size_t)(kBQ + kFwdGroups * 2 * kBK) * LD;
+  const size_t merge = (size_t)kBQ * LD + (size_t)kFwdGroups * kBQ * (DMAX + 2);
+  const size_t smem = (tiles > merge ? tiles : merge) * sizeof(float);
   auto kern = fwd_simt_kernel<T, DMAX>;
   cudaError_t e = ensure_smem(kern, (int)smem);
   if (e != cudaSuccess) return e;
   dim3 grid((a.Sq + kBQ - 1) / kBQ, a.H, a.B);
-  kern<<<grid, kThreads, smem, a.stream>>>(
+  kern<<<grid, kThreads * kFwdGroups, smem, a.stream>>>(
       (const T*)a.q, (const T*)a.k, (const T*)a.v, (T*)a.o, a.lse, a.H, a.Hkv, a.Sq, a.Sk, a.D,
       a.causal, a.sm_scale, a.kv_len, a.q_cos, a.q_sin, a.k_cos, a.k_sin, a.tbl_dtype, a.kv_lens, a.q_offs);
   return cudaGetLastError();
