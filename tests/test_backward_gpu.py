@@ -145,3 +145,37 @@ def test_tensor_core_grads_c2_shape_sampled():
     for t, w, name in ((tq.grad[:, sl], want[0], "dq"), (tk.grad[:, 3:4], want[1], "dk"),
                        (tv.grad[:, 3:4], want[2], "dv")):
         assert rel_err(to_np(t), w) < 2e-2, name
+
+
+@pytest.mark.parametrize("B,H,Hkv,S,causal,kv_len", [(4, 8, 2, 512, True, None), (3, 6, 3, 384, False, 301),
+                                                   (9, 4, 1, 256, True, None)])
+def test_ds_spill_path_matches_recompute_path(B, H, Hkv, S, causal, kv_len):
+    """pf_bwd with its full workspace (dK/dV spills dS; dQ is a GEMM over the spill,
+    pipelined over chunks of (batch, kv-head) units on two streams) against pf_bwd with a
+    delta-only workspace (dQ recomputes S and dP): dK/dV bit-identical (the same kernel),
+    dQ within bf16 summation-order noise; both against the oracle."""
+    from pallas_flash import _lib
+    from pallas_flash.flash_attention import _fwd
+    D = 128
+    q, k, v, do = (to_dev(x, torch.bfloat16) for x in inputs(B, H, Hkv, S, D, 11))
+    scale = 1.0 / np.sqrt(D)
+    kl = S if kv_len is None else kv_len
+    out, lse = _fwd(q, k, v, causal, scale, kl, True)
+    L = _lib.lib()
+    full = L.pf_bwd_workspace_size(1, B, H, Hkv, S, S, D, int(causal), kl)
+    ws = torch.empty(full, dtype=torch.uint8, device="cuda")
+    res = []
+    for nbytes in (full, B * H * S * 4):
+        g = [torch.empty_like(t) for t in (q, k, v)]
+        _lib.check(L.pf_bwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), do.data_ptr(),
+                            lse.data_ptr(), g[0].data_ptr(), g[1].data_ptr(), g[2].data_ptr(), 1, B, H, Hkv, S, S,
+                            D, int(causal), scale, kl, ws.data_ptr(), nbytes, _lib.stream_of(q)))
+        torch.cuda.synchronize()
+        res.append(g)
+    assert _lib.device_status(reset=True) == 0
+    assert torch.equal(res[0][1], res[1][1]) and torch.equal(res[0][2], res[1][2])
+    dq_s, dq_r = to_np(res[0][0]), to_np(res[1][0])
+    assert np.max(np.abs(dq_s - dq_r)) <= 2e-2 * max(1.0, float(np.max(np.abs(dq_r))))
+    rq, rk, rv = orc.attention_vjp(widen(q), widen(k), widen(v), widen(do), causal=causal, kv_len=kv_len)
+    for got, want in ((dq_s, rq), (to_np(res[0][1]), rk), (to_np(res[0][2]), rv)):
+        assert rel_err(got, want) < 2e-2

@@ -1182,7 +1182,7 @@ cudaError_t launch_dq_gemm_t(const BwdArgs& a) {
   cudaError_t e = ensure_smem(kern, Cfg::kSmem);
   if (e != cudaSuccess) return e;
   const int n_items = n_qt * BH;
-  const int grid = std::min(n_items, sm_count());
+  const int grid = std::min(n_items, a.dq_ctas > 0 ? a.dq_ctas : sm_count());
   kern<<<grid, Cfg::kThreads, Cfg::kSmem, a.stream>>>(tds, tk, (T*)a.dq, a.H, a.Hkv, a.Sq, a.kv_len, a.causal,
                                                     a.sm_scale, n_qt, n_items);
   return cudaGetLastError();

@@ -265,6 +265,10 @@ int pf_bwd(const void* q, const void* k, const void* v, const void* o, const voi
     const size_t spill = bwd_ds_spill_bytes(B, H, Sq, kv_len, a.causal);
     if (workspace_bytes >= need + spill) {
       a.ds_buf = reinterpret_cast<uint16_t*>(static_cast<uint8_t*>(workspace) + need);
+      // Measured and dropped: chunking the units and overlapping each chunk's dQ
+      // GEMM (side stream, small grid) with the next chunk's dK/dV -- a chunk of
+      // dK/dV CTAs is bound by its heaviest key tile, so the chunks' tails cost
+      // more than the overlap gains (2.2 vs 1.65 ms at config 2).
       st = cuda_status(launch_bwd_dkv_sm100(a), "pf_bwd (dkv + dS spill, tcgen05)");
       if (st != PF_OK) return st;
       return cuda_status(launch_bwd_dq_gemm_sm100(a), "pf_bwd (dq gemm, tcgen05)");

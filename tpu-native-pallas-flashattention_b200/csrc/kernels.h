@@ -35,6 +35,7 @@ struct BwdArgs {
   float sm_scale;
   float* dq_accum;  // f32 [B,H,Sq,D] scratch (tensor-core path)
   uint16_t* ds_buf;  // dS spill of the dK/dV kernel for the dQ GEMM (null: not written)
+  int dq_ctas;       // CTAs of the persistent dQ GEMM (0: one per SM)
   cudaStream_t stream;
 };
 
