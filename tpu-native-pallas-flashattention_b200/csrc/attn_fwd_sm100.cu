@@ -93,25 +93,33 @@ __device__ __forceinline__ void load8_table(const void* t, int dtype, long i, fl
 template <typename T, int D>
 __device__ __forceinline__ void rope_row_in_smem(uint8_t* tile, int row, const void* cos_t, const void* sin_t,
                                                  int tbl_dtype, long pos) {
-  constexpr int half = D / 2;
-#pragma unroll 1
-  for (int d0 = 0; d0 < half; d0 += 8) {
-    const int d1 = d0 + half;
+  constexpr int half = D / 2, NCH = half / 8;
+  // The table loads of chunk ch+1 are issued before chunk ch is rotated, so
+  // the row's eight (D = 128) global round trips overlap instead of queueing.
+  float c0[2][8], s0[2][8], c1[2][8], s1[2][8];
+  auto load = [&](int ch, int buf) {
+    const int d0 = ch * 8, d1 = d0 + half;
+    load8_table(cos_t, tbl_dtype, pos * D + d0, c0[buf]);
+    load8_table(sin_t, tbl_dtype, pos * D + d0, s0[buf]);
+    load8_table(cos_t, tbl_dtype, pos * D + d1, c1[buf]);
+    load8_table(sin_t, tbl_dtype, pos * D + d1, s1[buf]);
+  };
+  load(0, 0);
+#pragma unroll
+  for (int ch = 0; ch < NCH; ++ch) {
+    if (ch + 1 < NCH) load(ch + 1, (ch + 1) & 1);
+    const int buf = ch & 1;
+    const int d0 = ch * 8, d1 = d0 + half;
     uint4* p0 = reinterpret_cast<uint4*>(tile + (d0 >> 6) * (kBM * 128) + row * 128 + ((((d0 & 63) >> 3) ^ (row & 7)) << 4));
     uint4* p1 = reinterpret_cast<uint4*>(tile + (d1 >> 6) * (kBM * 128) + row * 128 + ((((d1 & 63) >> 3) ^ (row & 7)) << 4));
     uint4 v0 = *p0, v1 = *p1;
     T* x0 = reinterpret_cast<T*>(&v0);
     T* x1 = reinterpret_cast<T*>(&v1);
-    float c0[8], s0[8], c1[8], s1[8];
-    load8_table(cos_t, tbl_dtype, pos * D + d0, c0);
-    load8_table(sin_t, tbl_dtype, pos * D + d0, s0);
-    load8_table(cos_t, tbl_dtype, pos * D + d1, c1);
-    load8_table(sin_t, tbl_dtype, pos * D + d1, s1);
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
       const float a = to_f(x0[u]), bb = to_f(x1[u]);
-      x0[u] = from_f<T>(a * c0[u] - bb * s0[u]);
-      x1[u] = from_f<T>(bb * c1[u] + a * s1[u]);
+      x0[u] = from_f<T>(a * c0[buf][u] - bb * s0[buf][u]);
+      x1[u] = from_f<T>(bb * c1[buf][u] + a * s1[buf][u]);
     }
     *p0 = v0;
     *p1 = v1;
