@@ -29,6 +29,7 @@ namespace {
 constexpr int kKeysPerWarp = 32;
 constexpr int kSplitQuantum = 128;   // split lengths are multiples of this
 constexpr int kMaxSplitLen = 4096;
+constexpr int kSingleSplitLen = 1024;  // caches up to this length decode in one split
 
 template <typename T, int D>
 struct DecodeCfg {
@@ -463,6 +464,13 @@ __global__ void paged_gather_kernel(const uint16_t* pages, const int32_t* tables
 bool decode_supported(int D) { return D == 64 || D == 128 || D == 256; }
 
 void decode_plan(int max_len, int B, int Hkv, int* num_splits, int* split_len) {
+  if (max_len <= kSingleSplitLen) {
+    // Short caches (the generation decode step): one split, whose kernel writes
+    // the output itself, saves the combine launch on a launch-bound step.
+    *num_splits = 1;
+    *split_len = (max_len + kSplitQuantum - 1) / kSplitQuantum * kSplitQuantum;
+    return;
+  }
   const int units = B * Hkv;
   const int target = 4 * 148;
   int splits = (target + units - 1) / units;

@@ -129,7 +129,12 @@ decode_tc_kernel(DecodeArgs a, const __grid_constant__ CUtensorMap tm_k, const _
   if (len > a.max_len && split == 0 && threadIdx.x == 0) flag_status(PF_DEV_LEN_OVER_MAX);
   const int k_begin = split * a.split_len;
   const int k_end = min(len, k_begin + a.split_len);
-  if (k_begin >= k_end) return;  // uniform over the CTA
+  if (k_begin >= k_end) {  // uniform over the CTA
+    if (a.num_splits == 1)  // no combine follows: an empty sequence's output is 0
+      for (int e = threadIdx.x; e < gcount * D; e += blockDim.x)
+        static_cast<T*>(a.o)[((long)b * a.H + h0 + e / D) * D + e % D] = from_f<T>(0.f);
+    return;
+  }
 
   // Paged: every page id of the split is read (and validated) once, by all
   // threads in parallel, so the TMA issue below never waits on a global load.
@@ -380,6 +385,10 @@ decode_tc_kernel(DecodeArgs a, const __grid_constant__ CUtensorMap tm_k, const _
       L += r[D + 1] * sc;
       A += r[d] * sc;
     }
+    if (a.num_splits == 1) {  // the whole sequence: normalise and write the output
+      static_cast<T*>(a.o)[((long)b * a.H + h0 + g) * D + d] = from_f<T>(L == 0.f ? 0.f : A / L);
+      continue;
+    }
     float* out = a.partial + (((long)b * a.H + h0 + g) * a.num_splits + split) * (D + 2);
     out[d] = A;
     if (d == 0) {
@@ -428,7 +437,7 @@ cudaError_t launch_tc_t(const DecodeArgs& a) {
   else if (paired && seg_rows == 16) e = launch_tc_kernel<T, D, 16>(a, tk, tv, seg_rows, true);
   else e = launch_tc_kernel<T, D, kTileKeys>(a, tk, tv, seg_rows, paired);
   if (e != cudaSuccess) return e;
-  return launch_decode_combine(a);
+  return a.num_splits == 1 ? cudaSuccess : launch_decode_combine(a);
 }
 
 }  // namespace
