@@ -11,7 +11,9 @@
 //        S^T  = K Q^T         dP^T = V dO^T            (M = 128 keys, N = 128)
 //        dV  += P^T dO        dK  += dS^T Q             (A = P^T, dS^T from TMEM)
 //     With the dS spill (pf_bwd with room in its workspace) it also writes
-//     every 16-bit dS tile to global memory (TMA stores from a staging tile).
+//     every 16-bit dS tile to global memory, straight from registers, in the
+//     core-matrix layout the dQ GEMM's tensor core reads (one bulk copy per
+//     tile, no shared-memory staging on either side).
 //   dQ GEMM:      persistent; dQ of a 128-row query tile = scale * sum over its
 //     key tiles of dS K, streaming the spilled tiles (HBM-bound), so each
 //     (key tile, query tile) pair costs 5 tile GEMMs instead of 7.
@@ -75,35 +77,32 @@ struct BwdBars {
   uint64_t pv_done;                // dK/dV: dV(it) has read the P^T tile
   uint64_t p_half, ds_half;        // dK/dV: the first 32-column chunk of P^T / dS written
   uint64_t s_free, dp_free;        // S (dK/dV) / dP (dQ) loaded into registers
+  uint64_t stats_free[2];          // dK/dV: a column-statistics slot has been read
   uint64_t done;                   // accumulators final
   uint32_t tmem_base;
 };
 static_assert(sizeof(BwdBars) <= 256, "barrier block exceeds its shared-memory slot");
 
-// dK/dV with the dS spill: each elementwise warpgroup stages its 64-column
-// half of dS^T in the P^T tile once dV has read P^T, and one of its threads
-// sends it out with a TMA store.
-struct SpillBars {
-  uint64_t ds_written[2];  // the warpgroup's 128 threads wrote their dS^T rows
-  uint64_t ptile_free[2];  // the warpgroup's previous store finished reading the tile
-};
-
-// dK/dV: K, V resident; NS stages of (Q, dO) 128-row tiles plus their column statistics.
+// dK/dV: K, V resident; NQ stages of Q and NO of dO (128-row tiles), and two
+// slots of their column statistics.  Q is live from S(it) to dK(it), so a
+// third stage lets Q(it+1) load while Q(it-1) and Q(it) are still read; dO
+// (dP(it) to dV(it)) needs two.  A statistics slot is refilled once the
+// elementwise warps have read it (stats_free), not when its Q stage frees.
 template <int D>
 struct DkvCfg {
-  static constexpr int kNS = D == 128 ? 2 : 4;
+  static constexpr int kNQ = D == 128 ? 3 : 4;
+  static constexpr int kNO = D == 128 ? 2 : 4;
   static constexpr int kBoxes = D / 64;
   static constexpr int kTile = 128 * D * 2;
   static constexpr int kFixedOff = 0;
-  static constexpr int kStreamOff = 2 * kTile;
-  static constexpr int kStatOff = kStreamOff + kNS * 2 * kTile;  // [kNS][2][128] f32: -lse*log2e, -delta
-  static constexpr int kPOff = kStatOff + kNS * 256 * 4;   // P^T: 128 keys x 128 queries, SW128 K-major
-  static constexpr int kBarOff = kPOff + 128 * 128 * 2;
-  static constexpr int kSpillBarOff = kBarOff + 256;
+  static constexpr int kQOff = 2 * kTile;
+  static constexpr int kOOff = kQOff + kNQ * kTile;
+  static constexpr int kStatOff = kOOff + kNO * kTile;  // [2][2][128] f32: -lse*log2e, -delta
+  static constexpr int kBarOff = kStatOff + 2 * 256 * 4;
   // No alignment slack: at D = 128 the tiles fill the 227 KB limit, so the
   // kernel requires (and checks) a 1024-byte aligned dynamic shared window.
-  static constexpr int kSmem = kSpillBarOff + 64;
-  static_assert(kPOff % 1024 == 0, "P^T tile must be 1024-byte aligned");
+  static constexpr int kSmem = kBarOff + 256;
+  static_assert(kSmem <= 232448, "dK/dV shared memory exceeds the per-block limit");
   static constexpr uint32_t kS = 0, kDP = 128, kDV = 256, kDK = 256 + D;
 };
 
@@ -165,9 +164,13 @@ __device__ __forceinline__ void ds_chunk_keep16(const uint32_t (&rd)[32], const 
   tmem_st16(out, pk);
 }
 
-// dS spill layout: one 128 x 128 16-bit tile per live (key tile kt, query tile
-// qi) pair of a (batch, head) plane, rows = keys, columns = queries (row-major,
-// 256 B per row).  A plane's tiles are ordered by key tile, then query tile;
+// dS spill layout: one 128 x 128 16-bit tile (32 KiB) per live (key tile kt,
+// query tile qi) pair of a (batch, head) plane, stored as 8 x 8 core matrices
+// (8 keys x 8 queries, one key's 8 queries in 16 contiguous bytes): key k,
+// query q sits at byte (q / 8) * 2048 + k * 16 + (q % 8) * 2.  The tensor core
+// reads that as the MN-major, unswizzled A operand (M = queries, K = keys) of
+// dQ = dS K, and the 32 keys of a warp's TMEM lanes store 512 contiguous bytes
+// per 8-query group.  A plane's tiles are ordered by key tile, then query tile;
 // key tile kt has the query tiles [i0(kt), nq) with i0 = kt under the causal
 // mask (0 otherwise) and none when its first key is at or past kv_len.
 __host__ __device__ __forceinline__ long ds_tile_offset(int kt, int nq, int causal) {
@@ -231,17 +234,6 @@ __device__ __forceinline__ void load_cols(const float* src, float (&dst)[N]) {
   }
 }
 
-// Packed P of one 32-column chunk (columns [col, col + 32)) of key row `r`
-// into the P^T tile (two 128-byte-swizzled K-major boxes of 64 columns):
-// 16-byte chunk j of a box row lives at chunk position j ^ (r % 8).
-__device__ __forceinline__ void store_sw128_chunk(uint8_t* tile, int r, int col, const uint32_t (&pk)[16]) {
-  uint8_t* row = tile + (col / 64) * (128 * 128) + r * 128;
-  const int j0 = (col % 64) / 8;
-#pragma unroll
-  for (int q = 0; q < 4; ++q)
-    *reinterpret_cast<uint4*>(row + (((j0 + q) ^ (r & 7)) << 4)) =
-        make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-}
 
 
 // Writes an f32 accumulator row (TMEM columns [col0, col0 + n)) times `scale`
@@ -273,20 +265,19 @@ __device__ __forceinline__ void store_acc_row(uint32_t taddr, T* dst, int n, flo
 // ============================================================================
 // dK / dV
 // ============================================================================
-// PT: P stays in TMEM (packed over the consumed S tile) and dV is a TS MMA;
-// the shared-memory tile then only stages the dS spill.  Otherwise P^T goes
-// through that tile and dV is an SS MMA, which lets S(it+1) be issued as soon
-// as S(it) is in registers.
-template <typename T, int D, bool PT>
+// P stays in TMEM (packed over the consumed S tile) and dV is a TS MMA.  With
+// the spill (ds_buf != nullptr) every dS tile also goes to global memory
+// straight from the elementwise warps' registers.
+template <typename T, int D>
 __global__ void __launch_bounds__(EwDkv::kThreads, 1)
 bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                      const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
-                     const __grid_constant__ CUtensorMap tm_ds, int spill,
+                     uint8_t* __restrict__ ds_buf,
                      const float* __restrict__ lse, const float* __restrict__ delta,
                      T* __restrict__ dk, T* __restrict__ dv, int H, int Hkv,
                      int Sq, int Sk, int kv_len, int causal, float sm_scale, float scale_log2, int n_kt) {
   using Cfg = DkvCfg<D>;
-  constexpr int NS = Cfg::kNS;
+  constexpr int NQ = Cfg::kNQ, NO = Cfg::kNO;
   constexpr int kEWG = EwDkv::kEWG, kNCH = EwDkv::kNCH, kEWThreads = EwDkv::kEWThreads;
   constexpr int kCertWarp = EwDkv::kCertWarp;
   constexpr int FMT = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
@@ -300,7 +291,6 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
   }
   uint8_t* smem = smem_raw;
   BwdBars* bars = reinterpret_cast<BwdBars*>(smem + Cfg::kBarOff);
-  SpillBars* sp = reinterpret_cast<SpillBars*>(smem + Cfg::kSpillBarOff);
   const uint32_t sbase = smem_u32(smem);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
 
@@ -319,9 +309,11 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->fixed, 1);
-    for (int s = 0; s < NS; ++s) {
+    for (int s = 0; s < NQ; ++s) {
       mbar_init(&bars->full[s], 1 + 32);  // TMA tx arrive + the producer warp's 32 stat writers
       mbar_init(&bars->empty[s], 1);
+    }
+    for (int s = 0; s < NO; ++s) {
       mbar_init(&bars->vfull[s], 1);
       mbar_init(&bars->vempty[s], 1);
     }
@@ -329,15 +321,12 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
     mbar_init(&bars->dp_full, 1);
     mbar_init(&bars->p_ready, kEWThreads);
     mbar_init(&bars->ds_ready, kEWThreads + 1);  // + certifier: dO(it+1) landed
-    mbar_init(&bars->pv_done, 1);
     mbar_init(&bars->p_half, kEWThreads);
     mbar_init(&bars->ds_half, kEWThreads);
     mbar_init(&bars->s_free, kEWThreads + 1);  // + certifier: Q(it+1) and its statistics landed
+    mbar_init(&bars->stats_free[0], kEWThreads);
+    mbar_init(&bars->stats_free[1], kEWThreads);
     mbar_init(&bars->done, 1);
-    for (int w = 0; w < 2; ++w) {
-      mbar_init(&sp->ds_written[w], 128);
-      mbar_init(&sp->ptile_free[w], 1);
-    }
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -380,59 +369,60 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
       fetch_stats(0);
       int last_q = -1, last_do = -1;
       for (int it = 0; it < n_it; ++it) {
-        const int s = it % NS;
-        if (it >= NS && !mbar_wait(&bars->empty[s], ((it / NS) - 1) & 1)) break;
+        const int s = it % NQ, so = it % NO, ss = it & 1;
+        if (it >= NQ && !mbar_wait(&bars->empty[s], ((it / NQ) - 1) & 1)) break;
         if (lane == 0) trace(15, it - 1);
         const int g = it / nqi, qi = i0 + it % nqi;
         const int plane = b * H + hk * G + g;
-        uint8_t* qdst = smem + Cfg::kStreamOff + s * 2 * Cfg::kTile;
         if (lane == 0) {
           mbar_expect_tx(&bars->full[s], Cfg::kTile);
           for (int c = 0; c < Cfg::kBoxes; ++c)
-            tma_load_3d(qdst + c * 128 * 128, &tm_q, &bars->full[s], c * 64, qi * 128, plane);
+            tma_load_3d(smem + Cfg::kQOff + s * Cfg::kTile + c * 128 * 128, &tm_q, &bars->full[s], c * 64,
+                        qi * 128, plane);
         }
         last_q = it;
+        // The statistics slot of tile it - 2 has been read by its dS step.
+        if (it >= 2 && !mbar_wait(&bars->stats_free[ss], ((it >> 1) - 1) & 1)) break;
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          stats[s * 256 + lane + 32 * u] = pl[u];
-          stats[s * 256 + 128 + lane + 32 * u] = pd[u];
+          stats[ss * 256 + lane + 32 * u] = pl[u];
+          stats[ss * 256 + 128 + lane + 32 * u] = pd[u];
         }
         mbar_arrive(&bars->full[s]);
         if (it + 1 < n_it) fetch_stats(it + 1);
         // dO is needed later (by dP) and released earlier (after dV) than Q.
-        if (it >= NS && !mbar_wait(&bars->vempty[s], ((it / NS) - 1) & 1)) break;
+        if (it >= NO && !mbar_wait(&bars->vempty[so], ((it / NO) - 1) & 1)) break;
         if (lane == 0) {
-          mbar_expect_tx(&bars->vfull[s], Cfg::kTile);
+          mbar_expect_tx(&bars->vfull[so], Cfg::kTile);
           for (int c = 0; c < Cfg::kBoxes; ++c)
-            tma_load_3d(qdst + Cfg::kTile + c * 128 * 128, &tm_do, &bars->vfull[s], c * 64, qi * 128, plane);
+            tma_load_3d(smem + Cfg::kOOff + so * Cfg::kTile + c * 128 * 128, &tm_do, &bars->vfull[so], c * 64,
+                        qi * 128, plane);
         }
         last_do = it;
       }
       if (lane == 0) {  // exit drain: no copy may land after the CTA is gone
         mbar_wait(&bars->fixed, 0);
-        drain_ring(bars->full, NS, last_q);
-        drain_ring(bars->vfull, NS, last_do);
+        drain_ring(bars->full, NQ, last_q);
+        drain_ring(bars->vfull, NO, last_do);
       }
     }
   } else if (warp == 1) {
     // Tensor-core order per iteration:
-    //   [S(it) in registers] S(it+1)   [P(it) in smem] dV(it)   [dS(it) in TMEM] dK(it) dP(it+1)
+    //   dV(it) [P(it) in TMEM, in two halves]   S(it+1)   dK(it) [dS(it) in TMEM, two halves]   dP(it+1)
     // The elementwise warps release the S tile as soon as they have loaded
-    // it and write P^T to shared memory, so S(it+1) runs under the P
-    // arithmetic of tile it and the tensor core always has queued work (a
-    // burst issued to an idle tensor core pays several hundred cycles of
-    // latency).  dS stays in TMEM; dP(it+1) overwrites it only after dK(it)
-    // read it (the tensor core runs its queue in order).
+    // it, so S(it+1) queues behind dV(it) (which reads P over the S columns;
+    // the tensor core runs its queue in order) and runs under the dS
+    // arithmetic of tile it.  dS stays in TMEM; dP(it+1) overwrites it only
+    // after dK(it) read it.
     if (lane == 0 && n_it > 0) {
       bool ok = mbar_wait(&bars->fixed, 0);
       tc_fence_after();
       const uint32_t k_addr = sbase + Cfg::kFixedOff, v_addr = k_addr + Cfg::kTile;
       const uint64_t kd = desc_k_base<128>(k_addr), vd = desc_k_base<128>(v_addr);
-      const uint64_t pd = desc_k_base<128>(sbase + Cfg::kPOff);
-      auto stage = [&](int it) { return sbase + Cfg::kStreamOff + (it % NS) * 2 * Cfg::kTile; };
+      auto q_stage = [&](int it) { return sbase + Cfg::kQOff + (it % NQ) * Cfg::kTile; };
+      auto o_stage = [&](int it) { return sbase + Cfg::kOOff + (it % NO) * Cfg::kTile; };
       auto issue_s = [&](int it) {
-        const uint32_t q_addr = stage(it);
-        const uint64_t qd = desc_k_base<128>(q_addr);
+        const uint64_t qd = desc_k_base<128>(q_stage(it));
         umma_ss(tmem + Cfg::kS, kd, qd, idesc_s, 0);
 #pragma unroll
         for (int kk = 1; kk < D / 16; ++kk)
@@ -442,8 +432,7 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
       auto issue_dp = [&](int it) -> bool {
         if (it == 0 && !mbar_wait_spin(&bars->vfull[0], 0)) return false;  // later tiles: certified
         tc_fence_after();
-        const uint32_t do_addr = stage(it) + Cfg::kTile;
-        const uint64_t od = desc_k_base<128>(do_addr);
+        const uint64_t od = desc_k_base<128>(o_stage(it));
         umma_ss(tmem + Cfg::kDP, vd, od, idesc_s, 0);
 #pragma unroll
         for (int kk = 1; kk < D / 16; ++kk)
@@ -458,72 +447,36 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
         ok = issue_dp(0);
       }
       for (int it = 0; ok && it < n_it; ++it) {
-        const uint32_t q_addr = stage(it), do_addr = q_addr + Cfg::kTile;
-        // S(it+1) and the two halves of dV(it) are independent of each other
-        // (the halves only in order); issue whichever is ready first so a
-        // late Q tile does not hold back dV (bounded like every wait).  dV's
-        // k-steps {0,1,4,5} read the first 32-column chunk each elementwise
-        // warpgroup wrote (p_half), {2,3,6,7} the second (p_ready).
-        bool need_s = it + 1 < n_it, need_v1 = true, need_v2 = true;
-        const uint64_t t0 = global_timer_ns();
-        const uint64_t om = desc_mn_base<128>(do_addr);
-        if constexpr (PT) {
-          // dV(it) reads P from the S tile, so S(it+1) queues behind it.
-          ok = mbar_wait_spin(&bars->p_half, it & 1);
-          if (!ok) break;
-          tc_fence_after();
-          umma_ts(tmem + Cfg::kDV, tmem + Cfg::kS, om, idesc_acc, it > 0);
-          umma_ts_acc(tmem + Cfg::kDV, tmem + Cfg::kS + split_packed_col(1), om + mnoff(1), idesc_acc);
-          umma_ts_acc(tmem + Cfg::kDV, tmem + Cfg::kS + split_packed_col(4), om + mnoff(4), idesc_acc);
-          umma_ts_acc(tmem + Cfg::kDV, tmem + Cfg::kS + split_packed_col(5), om + mnoff(5), idesc_acc);
-          ok = mbar_wait_spin(&bars->p_ready, it & 1);
-          if (!ok) break;
-          tc_fence_after();
-          umma_ts_acc(tmem + Cfg::kDV, tmem + Cfg::kS + split_packed_col(2), om + mnoff(2), idesc_acc);
-          umma_ts_acc(tmem + Cfg::kDV, tmem + Cfg::kS + split_packed_col(3), om + mnoff(3), idesc_acc);
-          umma_ts_acc(tmem + Cfg::kDV, tmem + Cfg::kS + split_packed_col(6), om + mnoff(6), idesc_acc);
-          umma_ts_acc(tmem + Cfg::kDV, tmem + Cfg::kS + split_packed_col(7), om + mnoff(7), idesc_acc);
-          umma_commit(&bars->vempty[it % NS]);
-          if (need_s) {
-            ok = mbar_wait_spin(&bars->s_free, it & 1);  // Q(it+1) certified
-            if (!ok) break;
-            tc_fence_after();
-            issue_s(it + 1);
-          }
-          need_s = need_v2 = false;
-        }
-        for (uint32_t spin = 1; ok && (need_s || need_v2); ++spin) {
-          if (need_s && mbar_test(&bars->s_free, it & 1)) {  // Q(it+1) certified in the phase
-            trace(14, it);
-            tc_fence_after();
-            issue_s(it + 1);
-            need_s = false;
-          } else if (need_v1 && mbar_test(&bars->p_half, it & 1)) {
-            trace(1, it);
-            tc_fence_after();
-            umma_ss(tmem + Cfg::kDV, pd, om, idesc_acc, it > 0);
-            umma_ss_acc(tmem + Cfg::kDV, pd + koff<128>(1), om + mnoff(1), idesc_acc);
-            umma_ss_acc(tmem + Cfg::kDV, pd + koff<128>(4), om + mnoff(4), idesc_acc);
-            umma_ss_acc(tmem + Cfg::kDV, pd + koff<128>(5), om + mnoff(5), idesc_acc);
-            need_v1 = false;
-          } else if (!need_v1 && need_v2 && mbar_test(&bars->p_ready, it & 1)) {
-            tc_fence_after();
-            umma_ss_acc(tmem + Cfg::kDV, pd + koff<128>(2), om + mnoff(2), idesc_acc);
-            umma_ss_acc(tmem + Cfg::kDV, pd + koff<128>(3), om + mnoff(3), idesc_acc);
-            umma_ss_acc(tmem + Cfg::kDV, pd + koff<128>(6), om + mnoff(6), idesc_acc);
-            umma_ss_acc(tmem + Cfg::kDV, pd + koff<128>(7), om + mnoff(7), idesc_acc);
-            umma_commit(&bars->pv_done);
-            umma_commit(&bars->vempty[it % NS]);
-            need_v2 = false;
-          } else if ((spin & 1023u) == 0 && global_timer_ns() - t0 > *(volatile unsigned long long*)&g_wait_limit_ns) {
-            flag_status(PF_DEV_WAIT_TIMEOUT);
-            ok = false;
-          }
-        }
+        // dV(it) in two halves: k-steps {0,1,4,5} read the first 32-column
+        // chunk each elementwise warpgroup wrote (p_half), {2,3,6,7} the
+        // second (p_ready).
+        const uint64_t om = desc_mn_base<128>(o_stage(it));
+        ok = mbar_wait_spin(&bars->p_half, it & 1);
         if (!ok) break;
+        trace(1, it);
+        tc_fence_after();
+        umma_ts(tmem + Cfg::kDV, tmem + Cfg::kS, om, idesc_acc, it > 0);
+        umma_ts_acc(tmem + Cfg::kDV, tmem + Cfg::kS + split_packed_col(1), om + mnoff(1), idesc_acc);
+        umma_ts_acc(tmem + Cfg::kDV, tmem + Cfg::kS + split_packed_col(4), om + mnoff(4), idesc_acc);
+        umma_ts_acc(tmem + Cfg::kDV, tmem + Cfg::kS + split_packed_col(5), om + mnoff(5), idesc_acc);
+        ok = mbar_wait_spin(&bars->p_ready, it & 1);
+        if (!ok) break;
+        tc_fence_after();
+        umma_ts_acc(tmem + Cfg::kDV, tmem + Cfg::kS + split_packed_col(2), om + mnoff(2), idesc_acc);
+        umma_ts_acc(tmem + Cfg::kDV, tmem + Cfg::kS + split_packed_col(3), om + mnoff(3), idesc_acc);
+        umma_ts_acc(tmem + Cfg::kDV, tmem + Cfg::kS + split_packed_col(6), om + mnoff(6), idesc_acc);
+        umma_ts_acc(tmem + Cfg::kDV, tmem + Cfg::kS + split_packed_col(7), om + mnoff(7), idesc_acc);
+        umma_commit(&bars->vempty[it % NO]);
+        if (it + 1 < n_it) {
+          ok = mbar_wait_spin(&bars->s_free, it & 1);  // Q(it+1) certified
+          if (!ok) break;
+          tc_fence_after();
+          issue_s(it + 1);
+          trace(14, it);
+        }
         trace(2, it);
         // dK(it) in the same two halves (ds_half, then ds_ready).
-        const uint64_t qm = desc_mn_base<128>(q_addr);
+        const uint64_t qm = desc_mn_base<128>(q_stage(it));
         ok = mbar_wait_spin(&bars->ds_half, it & 1);
         if (!ok) break;
         tc_fence_after();
@@ -539,7 +492,7 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
         umma_ts_acc(tmem + Cfg::kDK, tmem + Cfg::kDP + split_packed_col(3), qm + mnoff(3), idesc_acc);
         umma_ts_acc(tmem + Cfg::kDK, tmem + Cfg::kDP + split_packed_col(6), qm + mnoff(6), idesc_acc);
         umma_ts_acc(tmem + Cfg::kDK, tmem + Cfg::kDP + split_packed_col(7), qm + mnoff(7), idesc_acc);
-        umma_commit(&bars->empty[it % NS]);
+        umma_commit(&bars->empty[it % NQ]);
         if (it + 1 < n_it && !(ok = issue_dp(it + 1))) break;
         trace(4, it);
       }
@@ -550,10 +503,10 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
       bool ok = true;
       for (int it = 0; ok && it < n_it; ++it) {
         const bool next = it + 1 < n_it;
-        if (next) ok = mbar_wait(&bars->full[(it + 1) % NS], ((it + 1) / NS) & 1);
+        if (next) ok = mbar_wait(&bars->full[(it + 1) % NQ], ((it + 1) / NQ) & 1);
         if (!ok) break;
         mbar_arrive(&bars->s_free);
-        if (next) ok = mbar_wait(&bars->vfull[(it + 1) % NS], ((it + 1) / NS) & 1);
+        if (next) ok = mbar_wait(&bars->vfull[(it + 1) % NO], ((it + 1) / NO) & 1);
         if (!ok) break;
         mbar_arrive(&bars->ds_ready);
         // Never arrive twice in one phase.
@@ -568,21 +521,23 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
     const int kpos = k0 + row;
     const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
     const bool key_ok = kpos < kv_len;
-    const bool spill_issuer = spill && warp == 2 + 4 * cw && lane == 0;  // sends the warpgroup's dS^T half
-    const bool tr = lane == 0 && quad == 2 && cw < 2;  // trace writers
+    const bool tr = lane == 0 && quad == 2 && cw == 0;  // trace writer
     const float2 sc2 = make_float2(scale_log2, scale_log2);
+    const long plane_tiles = ds_tiles_per_plane(nq, kv_len, causal);
+    const long kt_tiles = ds_tile_offset(kt, nq, causal);
+    const uint64_t ds_pol = l2_evict_first_policy();
     bool ok = true;
     for (int it = 0; ok && it < n_it; ++it) {
-      const int st = it % NS;
+      const int st = it % NQ, ss = it & 1;
       const int qc = (i0 + it % nqi) * 128 + col0;  // first query column of this thread
-      // The stage's statistics were written by the producer warp before its
-      // arrive on full[st]; the stage is not refilled before dK(it) retires.
+      // The slot's statistics were written by the producer warp before its
+      // arrive on full[st]; the slot is not refilled before stats_free.
       // Loading them before the S wait keeps their latency off the critical path.
-      if (!mbar_wait(&bars->full[st], (it / NS) & 1)) { ok = false; break; }
+      if (!mbar_wait(&bars->full[st], (it / NQ) & 1)) { ok = false; break; }
       float nl2[kNCH * 32];
-      load_cols<kNCH * 32>(stats + st * 256 + col0, nl2);
+      load_cols<kNCH * 32>(stats + ss * 256 + col0, nl2);
       if (!mbar_wait_spin(&bars->s_full[0], it & 1)) { ok = false; break; }
-      if (tr) trace(8 + 3 * cw, it);
+      if (tr) trace(8, it);
       tc_fence_after();
       uint32_t keep[kNCH][16], pk[kNCH][16];
       {
@@ -591,8 +546,7 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
         tmem_wait_ld();
         tc_fence_before();
         mbar_arrive(&bars->s_free);  // S(it+1) may now overwrite the tile
-        if (tr && cw == 0) trace(5, it);
-        // Chunk by chunk: P^T of a thread's first chunk is published (p_half)
+        // Chunk by chunk: P of a thread's first chunk is published (p_half)
         // before the second is computed, so dV can start on half the queries.
         static_assert(kNCH == 2, "the two-phase P / dS publication assumes two chunks per thread");
 #pragma unroll
@@ -607,77 +561,60 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
               return key_ok && qp < Sq && (!causal || qp >= kpos);
             });
           }
-          if constexpr (PT) {
-            // P packed over the chunk's own (consumed) S columns: the A operand of dV.
-            tmem_st16(lane_base + Cfg::kS + col0 + 32 * h, pk[h]);
-            if (h == 0) {
-              tmem_wait_st();
-              tc_fence_before();
-              mbar_arrive(&bars->p_half);
-            }
-          } else {
-            // The P^T tile is single-buffered: dV(it-1) must have read it.
-            if (h == 0 && it > 0 && !mbar_wait_spin(&bars->pv_done, (it - 1) & 1)) { ok = false; break; }
-            store_sw128_chunk(smem + Cfg::kPOff, row, col0 + 32 * h, pk[h]);
-            fence_proxy_async_smem();
-            if (h == 0) mbar_arrive(&bars->p_half);
+          // P packed over the chunk's own (consumed) S columns: the A operand of dV.
+          tmem_st16(lane_base + Cfg::kS + col0 + 32 * h, pk[h]);
+          if (h == 0) {
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(&bars->p_half);
           }
         }
-        if (!ok) break;
-        if (tr && cw == 0) trace(6, it);
       }
-      if (tr && cw == 0) trace(7, it);
-      if constexpr (PT) tmem_wait_st();
+      if (tr) trace(7, it);
+      tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&bars->p_ready);
       float nd[kNCH * 32];
-      load_cols<kNCH * 32>(stats + st * 256 + 128 + col0, nd);
-      if (tr) trace(9 + 3 * cw, it);
+      load_cols<kNCH * 32>(stats + ss * 256 + 128 + col0, nd);
+      mbar_arrive(&bars->stats_free[ss]);  // release: the slot's loads are done
+      if (tr) trace(9, it);
       if (!mbar_wait_spin(&bars->dp_full, it & 1)) { ok = false; break; }
+      if (tr) trace(0, it);
       tc_fence_after();
+      // This thread's key row of the spilled tile: 8-query group q8 at q8 * 2048 + row * 16.
+      uint8_t* ds_row = ds_buf != nullptr
+                            ? ds_buf + ((long)(b * H + hk * G + it / nqi) * plane_tiles + kt_tiles + it % nqi) *
+                                           (128 * 128 * 2) + row * 16
+                            : nullptr;
+      // Each chunk's spill stores follow the barrier that lets dK read it.
+      auto spill = [&](int h, const uint32_t (&pkd)[16]) {
+        if (ds_row == nullptr) return;
+#pragma unroll
+        for (int g = 0; g < 4; ++g)
+          st_global_hint(ds_row + ((col0 + 32 * h) / 8 + g) * 2048,
+                         make_uint4(pkd[4 * g], pkd[4 * g + 1], pkd[4 * g + 2], pkd[4 * g + 3]), ds_pol);
+      };
+      uint32_t pkd[kNCH][16];
 #pragma unroll
       for (int h = 0; h < kNCH; ++h) {
-        uint32_t rd[32], pkd[16];
+        uint32_t rd[32];
         tmem_ld32(lane_base + Cfg::kDP + col0 + 32 * h, rd);
         tmem_wait_ld();
         ds_chunk_keep16<FMT>(rd, keep[h], [&](int c) { return make_float2(nd[32 * h + c], nd[32 * h + c + 1]); },
-                             lane_base + Cfg::kDP + col0 + 32 * h, pkd);
+                             lane_base + Cfg::kDP + col0 + 32 * h, pkd[h]);
         if (h == 0) {  // first chunk of dS in place: dK may start on it
           tmem_wait_st();
           tc_fence_before();
           mbar_arrive(&bars->ds_half);
-        }
-        if (spill) {  // dS^T rows into the staging tile once the previous store has read it
-          if (h == 0 && it > 0) {
-            if (spill_issuer) {
-              bulk_wait_read_all();
-              mbar_arrive(&sp->ptile_free[cw]);
-            }
-            if (!mbar_wait_spin(&sp->ptile_free[cw], (it - 1) & 1)) { ok = false; break; }
-          }
-          store_sw128_chunk(smem + Cfg::kPOff, row, col0 + 32 * h, pkd);
+          spill(0, pkd[0]);
         }
       }
-      if (!ok) break;
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&bars->ds_ready);
-      if (spill) {
-        fence_proxy_async_smem();
-        mbar_arrive(&sp->ds_written[cw]);
-        if (spill_issuer) {
-          if (!mbar_wait(&sp->ds_written[cw], it & 1)) { ok = false; break; }
-          const long plane = (long)b * H + hk * G + it / nqi;
-          const long tile = plane * ds_tiles_per_plane(nq, kv_len, causal) + ds_tile_offset(kt, nq, causal) +
-                            it % nqi;
-          tma_store_3d_hint(&tm_ds, smem + Cfg::kPOff + cw * (128 * 128), col0, 0, (int)tile,
-                            l2_evict_first_policy());
-          bulk_commit_group();
-        }
-      }
-      if (tr) trace(10 + 3 * cw, it);
+      spill(1, pkd[1]);
+      if (tr) trace(10, it);
     }
-    if (spill_issuer) bulk_wait_all();  // the dS stores complete before the CTA exits
     // Epilogue: the first half of the warpgroups writes dV, the second half
     // dK (scaled), each a contiguous slice of the D columns.
     const bool have = n_it > 0 && ok && mbar_wait(&bars->done, 0);
@@ -984,7 +921,7 @@ __device__ __forceinline__ int dq_gemm_item(int r, int cta, int ctas) {
 
 template <typename T, int D>
 __global__ void __launch_bounds__(DqGemmCfg<D>::kThreads, 1)
-bwd_dq_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tm_ds, const __grid_constant__ CUtensorMap tm_k,
+bwd_dq_gemm_sm100_kernel(const uint8_t* __restrict__ ds_buf, const __grid_constant__ CUtensorMap tm_k,
                          T* __restrict__ dq, int H, int Hkv, int Sq, int kv_len, int causal, float sm_scale,
                          int n_qt, int n_items) {
   using Cfg = DqGemmCfg<D>;
@@ -1044,8 +981,8 @@ bwd_dq_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tm_ds, const __grid
           uint8_t* dst = smem + s * Cfg::kStage;
           const long tile = (long)bh * plane_tiles + ds_tile_offset(it, n_qt, causal) + (qt - (causal ? it : 0));
           mbar_expect_tx(&bars->full[s], Cfg::kStage);
-          for (int c = 0; c < 2; ++c)  // read once: evict first
-            tma_load_3d_hint(dst + c * 128 * 128, &tm_ds, &bars->full[s], c * 64, 0, (int)tile, pol);
+          // The spilled tile is already in the tensor core's operand layout: one bulk copy (read once: evict first).
+          bulk_load_hint(dst, ds_buf + tile * Cfg::kDsTile, Cfg::kDsTile, &bars->full[s], pol);
           for (int c = 0; c < Cfg::kBoxes; ++c)
             tma_load_3d(dst + Cfg::kDsTile + c * 128 * 128, &tm_k, &bars->full[s], c * 64, it * 128, kvp);
           last = g;
@@ -1070,10 +1007,12 @@ bwd_dq_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tm_ds, const __grid
           if (!mbar_wait_spin(&bars->full[s], (g / NS) & 1)) { ok = false; break; }
           tc_fence_after();
           const uint32_t ds_addr = sbase + s * Cfg::kStage;
-          const uint64_t ad = desc_mn_base<128>(ds_addr), bd = desc_mn_base<128>(ds_addr + Cfg::kDsTile);
+          // A = dS: MN-major, unswizzled; 8-key groups 128 B apart (LBO), 8-query groups 2048 B apart (SBO);
+          // k-step kk (16 keys) starts 256 B further.
+          const uint64_t ad = smem_desc_noswz(ds_addr, 128, 2048), bd = desc_mn_base<128>(ds_addr + Cfg::kDsTile);
           umma_ss(acc, ad, bd, idesc, it > 0);
 #pragma unroll
-          for (int kk = 1; kk < 8; ++kk) umma_ss_acc(acc, ad + mnoff(kk), bd + mnoff(kk), idesc);
+          for (int kk = 1; kk < 8; ++kk) umma_ss_acc(acc, ad + (uint64_t)(kk * 256 >> 4), bd + mnoff(kk), idesc);
           umma_commit(&bars->empty[s]);
         }
         if (!ok) break;
@@ -1113,38 +1052,26 @@ bwd_dq_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tm_ds, const __grid
   }
 }
 
-template <typename T, int D, bool PT>
-cudaError_t launch_dkv_pt(const BwdArgs& a) {
+template <typename T, int D>
+cudaError_t launch_dkv_t(const BwdArgs& a) {
   using Cfg = DkvCfg<D>;
-  CUtensorMap tk, tv, tq, tdo, tds;
+  CUtensorMap tk, tv, tq, tdo;
   const int BH = a.B * a.H, BHk = a.B * a.Hkv;
   if (!make_tile_map(&tk, a.k, a.dtype, D, a.kv_len, a.Sk, BHk, 128) ||
       !make_tile_map(&tv, a.v, a.dtype, D, a.kv_len, a.Sk, BHk, 128) ||
       !make_tile_map(&tq, a.q, a.dtype, D, a.Sq, a.Sq, BH, 128) ||
       !make_tile_map(&tdo, a.dout, a.dtype, D, a.Sq, a.Sq, BH, 128))
     return cudaErrorInvalidValue;
-  const int spill = a.ds_buf != nullptr;
-  tds = tk;  // unused without the spill
-  if (spill) {
-    const long tiles = (long)BH * ds_tiles_per_plane((a.Sq + 127) / 128, a.kv_len, a.causal);
-    if (tiles <= 0 || tiles > INT_MAX || !make_tile_map(&tds, a.ds_buf, a.dtype, 128, 128, 128, (int)tiles, 128))
-      return cudaErrorInvalidValue;
-  }
-  auto kern = bwd_dkv_sm100_kernel<T, D, PT>;
+  if (a.ds_buf != nullptr && (reinterpret_cast<uintptr_t>(a.ds_buf) & 15)) return cudaErrorInvalidValue;
+  auto kern = bwd_dkv_sm100_kernel<T, D>;
   cudaError_t e = ensure_smem(kern, Cfg::kSmem);
   if (e != cudaSuccess) return e;
   const int n_kt = (a.Sk + 127) / 128;
-  kern<<<n_kt * BHk, EwDkv::kThreads, Cfg::kSmem, a.stream>>>(tk, tv, tq, tdo, tds, spill, a.lse, a.delta,
-                                                       (T*)a.dk, (T*)a.dv, a.H, a.Hkv, a.Sq, a.Sk, a.kv_len,
-                                                       a.causal, a.sm_scale, a.sm_scale * kLog2e, n_kt);
+  kern<<<n_kt * BHk, EwDkv::kThreads, Cfg::kSmem, a.stream>>>(tk, tv, tq, tdo, reinterpret_cast<uint8_t*>(a.ds_buf),
+                                                       a.lse, a.delta, (T*)a.dk, (T*)a.dv, a.H, a.Hkv, a.Sq,
+                                                       a.Sk, a.kv_len, a.causal, a.sm_scale, a.sm_scale * kLog2e,
+                                                       n_kt);
   return cudaGetLastError();
-}
-
-template <typename T, int D>
-cudaError_t launch_dkv_t(const BwdArgs& a) {
-  // P in TMEM (TS dV) measured faster with and without the spill (config 2,
-  // same box: 1017 vs 1099 us without it); the SS-dV variant stays for comparison.
-  return launch_dkv_pt<T, D, true>(a);
 }
 
 template <typename T, int D>
@@ -1174,16 +1101,15 @@ cudaError_t launch_dq_gemm_t(const BwdArgs& a) {
   const int n_qt = (a.Sq + 127) / 128;
   const long tiles = (long)BH * ds_tiles_per_plane(n_qt, a.kv_len, a.causal);
   if (tiles <= 0 || tiles > INT_MAX) return cudaErrorInvalidValue;
-  CUtensorMap tds, tk;
-  if (!make_tile_map(&tds, a.ds_buf, a.dtype, 128, 128, 128, (int)tiles, 128) ||
-      !make_tile_map(&tk, a.k, a.dtype, D, a.kv_len, a.Sk, BHk, 128))
+  CUtensorMap tk;
+  if ((reinterpret_cast<uintptr_t>(a.ds_buf) & 15) || !make_tile_map(&tk, a.k, a.dtype, D, a.kv_len, a.Sk, BHk, 128))
     return cudaErrorInvalidValue;
   auto kern = bwd_dq_gemm_sm100_kernel<T, D>;
   cudaError_t e = ensure_smem(kern, Cfg::kSmem);
   if (e != cudaSuccess) return e;
   const int n_items = n_qt * BH;
   const int grid = std::min(n_items, a.dq_ctas > 0 ? a.dq_ctas : sm_count());
-  kern<<<grid, Cfg::kThreads, Cfg::kSmem, a.stream>>>(tds, tk, (T*)a.dq, a.H, a.Hkv, a.Sq, a.kv_len, a.causal,
+  kern<<<grid, Cfg::kThreads, Cfg::kSmem, a.stream>>>(reinterpret_cast<const uint8_t*>(a.ds_buf), tk, (T*)a.dq, a.H, a.Hkv, a.Sq, a.kv_len, a.causal,
                                                     a.sm_scale, n_qt, n_items);
   return cudaGetLastError();
 }

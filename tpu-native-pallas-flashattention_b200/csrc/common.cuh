@@ -224,6 +224,21 @@ __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gmem_src, 
       : "memory");
 }
 
+// Bulk copy with an L2 cache policy (e.g. evict first for data read once).
+__device__ __forceinline__ void bulk_load_hint(void* smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar,
+                                               uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
+      ::"r"(smem_u32(smem_dst)), "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+// 16-byte global store with an L2 cache policy.
+__device__ __forceinline__ void st_global_hint(void* dst, uint4 v, uint64_t policy) {
+  asm volatile("st.global.L2::cache_hint.v4.b32 [%0], {%1, %2, %3, %4}, %5;"
+               ::"l"(dst), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w), "l"(policy)
+               : "memory");
+}
+
 // ---------------------------------------------------------------------------
 // tcgen05: tensor memory and the 5th-generation tensor-core MMA
 // ---------------------------------------------------------------------------
@@ -359,6 +374,19 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t start, uint32_t lbo
   d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
   d |= (uint64_t)1 << 46;  // descriptor version for sm_100
   d |= (uint64_t)2 << 61;  // layout: SWIZZLE_128B
+  return d;
+}
+
+// Descriptor of an operand without swizzle ("interleaved" core matrices of
+// 8 rows x 16 bytes, 128 contiguous bytes each).  For an MN-major operand,
+// lbo is the byte step between core matrices along K (8-row groups) and sbo
+// the step between core matrices along M/N.
+__device__ __forceinline__ uint64_t smem_desc_noswz(uint32_t start, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((start >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;  // descriptor version for sm_100; layout 0: no swizzle
   return d;
 }
 
