@@ -142,11 +142,20 @@ int pf_bwd_dkv(const void* q, const void* k, const void* v, const void* dout,
  * delta (B*H*Sq f32) and, on the tensor-core path, the dS spill: every 16-bit
  * 128 x 128 dS tile the dK/dV kernel computes, from which dQ is one GEMM per
  * query tile instead of a kernel that recomputes S and dP.
- * pf_bwd_workspace_size returns the size with the spill (for these causal /
- * kv_len arguments; kv_len <= 0 means Sk); pf_bwd accepts any workspace of at
- * least the delta size and recomputes when the spill does not fit. */
+ * For problems with fewer key tiles (B*Hkv*ceil(Sk/128)) than the device has
+ * SMs, the dK/dV kernel splits each kv group's q heads over
+ * pf_bwd_head_parts() CTAs per key tile; the workspace then also holds their
+ * f32 partial dK/dV (summed in a fixed order, so results stay deterministic).
+ * pf_bwd_workspace_size returns the size with the spill and the partials (for
+ * these causal / kv_len arguments; kv_len <= 0 means Sk); pf_bwd accepts any
+ * workspace of at least the delta size, recomputes when the spill does not
+ * fit and does not split when the partials do not. */
 size_t pf_bwd_workspace_size(int dtype, int B, int H, int Hkv, int Sq, int Sk,
                              int D, int causal, int kv_len);
+/* q-head parts per key tile of that split on the current device (1: none).
+ * No reference counterpart: the Pallas grid has no analogue of this
+ * small-problem load balancing. */
+int pf_bwd_head_parts(int B, int H, int Hkv, int Sk);
 int pf_bwd(const void* q, const void* k, const void* v, const void* o,
            const void* dout, const float* lse, void* dq, void* dk, void* dv,
            int dtype, int B, int H, int Hkv, int Sq, int Sk, int D,

@@ -262,17 +262,42 @@ __device__ __forceinline__ void store_acc_row(uint32_t taddr, T* dst, int n, flo
   }
 }
 
+// The thread's TMEM lane row of n f32 accumulator columns, times `scale`, to
+// an f32 row (the head-split partial sums), or zeros when `zero`.
+__device__ __forceinline__ void store_acc_row_f32(uint32_t taddr, float* dst, int n, float scale, bool zero,
+                                                  bool write) {
+  for (int c = 0; c < n; c += 32) {
+    uint32_t r[32];
+    if (!zero) {
+      tmem_ld32(taddr + c, r);
+      tmem_wait_ld();
+    }
+    if (write) {
+      float4* d4 = reinterpret_cast<float4*>(dst + c);
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        d4[i] = zero ? make_float4(0.f, 0.f, 0.f, 0.f)
+                     : make_float4(__uint_as_float(r[4 * i]) * scale, __uint_as_float(r[4 * i + 1]) * scale,
+                                   __uint_as_float(r[4 * i + 2]) * scale, __uint_as_float(r[4 * i + 3]) * scale);
+    }
+  }
+}
+
 // ============================================================================
 // dK / dV
 // ============================================================================
 // P stays in TMEM (packed over the consumed S tile) and dV is a TS MMA.  With
 // the spill (ds_buf != nullptr) every dS tile also goes to global memory
 // straight from the elementwise warps' registers.
+// Head split (parts > 1, for problems with fewer key tiles than SMs): the q
+// heads of a kv group are divided over `parts` CTAs per key tile, each of
+// which writes its f32 partial dV and scaled dK to `part` ([2][parts][B*Hkv,
+// Sk, D]); dkv_part_reduce_kernel sums them in a fixed order.
 template <typename T, int D>
 __global__ void __launch_bounds__(EwDkv::kThreads, 1)
 bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                      const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
-                     uint8_t* __restrict__ ds_buf,
+                     uint8_t* __restrict__ ds_buf, float* __restrict__ part, int parts,
                      const float* __restrict__ lse, const float* __restrict__ delta,
                      T* __restrict__ dk, T* __restrict__ dv, int H, int Hkv,
                      int Sq, int Sk, int kv_len, int causal, float sm_scale, float scale_log2, int n_kt) {
@@ -295,17 +320,19 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
 
   // Causal: heaviest (first) key tiles of every head first.
-  const int BHk = gridDim.x / n_kt;
-  const int kt = blockIdx.x / BHk;
-  const int bhk = blockIdx.x % BHk;
+  const int units = gridDim.x / n_kt;  // (batch, kv head, head part) per key tile
+  const int BHk = units / parts;
+  const int kt = blockIdx.x / units;
+  const int bhk = (blockIdx.x % units) / parts, hp = (blockIdx.x % units) % parts;
   const int b = bhk / Hkv, hk = bhk % Hkv;
-  const int G = H / Hkv;
+  const int G = H / Hkv, Gp = G / parts;
+  const int g0 = hk * G + hp * Gp;  // first q head of this CTA, within the batch
   const int k0 = kt * 128;
   const int nq = (Sq + 127) / 128;
   int i0 = causal ? k0 / 128 : 0;
   if (k0 >= kv_len) i0 = nq;  // no live key in this tile
   const int nqi = max(0, nq - i0);
-  const int n_it = G * nqi;
+  const int n_it = Gp * nqi;
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->fixed, 1);
@@ -356,7 +383,7 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
       // latency stays off the Q barrier.
       float pl[4], pd[4];
       auto fetch_stats = [&](int it) {
-        const int plane = b * H + hk * G + it / nqi;
+        const int plane = b * H + g0 + it / nqi;
         const int qi = i0 + it % nqi;
         const long srow = (long)plane * Sq;
 #pragma unroll
@@ -372,8 +399,8 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
         const int s = it % NQ, so = it % NO, ss = it & 1;
         if (it >= NQ && !mbar_wait(&bars->empty[s], ((it / NQ) - 1) & 1)) break;
         if (lane == 0) trace(15, it - 1);
-        const int g = it / nqi, qi = i0 + it % nqi;
-        const int plane = b * H + hk * G + g;
+        const int qi = i0 + it % nqi;
+        const int plane = b * H + g0 + it / nqi;
         if (lane == 0) {
           mbar_expect_tx(&bars->full[s], Cfg::kTile);
           for (int c = 0; c < Cfg::kBoxes; ++c)
@@ -583,7 +610,7 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
       tc_fence_after();
       // This thread's key row of the spilled tile: 8-query group q8 at q8 * 2048 + row * 16.
       uint8_t* ds_row = ds_buf != nullptr
-                            ? ds_buf + ((long)(b * H + hk * G + it / nqi) * plane_tiles + kt_tiles + it % nqi) *
+                            ? ds_buf + ((long)(b * H + g0 + it / nqi) * plane_tiles + kt_tiles + it % nqi) *
                                            (128 * 128 * 2) + row * 16
                             : nullptr;
       // Each chunk's spill stores follow the barrier that lets dK read it.
@@ -622,13 +649,22 @@ bwd_dkv_sm100_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
     const bool write = kpos < Sk;
     const long orow = ((long)(b * Hkv + hk) * Sk + kpos) * D;
     constexpr int kHalf = kEWG / 2, kCols = D / kHalf;
-    const int part = cw % kHalf;
-    if (cw < kHalf)
-      store_acc_row<T, FMT>(lane_base + Cfg::kDV + part * kCols, dv + orow + part * kCols, kCols, 1.f, !have,
+    const int cpart = cw % kHalf;
+    if (parts > 1) {
+      // f32 partial rows: [dV | dK][hp][b * Hkv + hk][kpos][D]
+      const size_t plane_elems = (size_t)parts * BHk * Sk * D;
+      float* prow = part + ((size_t)hp * BHk + bhk) * Sk * D + (size_t)kpos * D + cpart * kCols;
+      if (cw < kHalf)
+        store_acc_row_f32(lane_base + Cfg::kDV + cpart * kCols, prow, kCols, 1.f, !have, write);
+      else
+        store_acc_row_f32(lane_base + Cfg::kDK + cpart * kCols, prow + plane_elems, kCols, sm_scale, !have, write);
+    } else if (cw < kHalf) {
+      store_acc_row<T, FMT>(lane_base + Cfg::kDV + cpart * kCols, dv + orow + cpart * kCols, kCols, 1.f, !have,
                             write);
-    else
-      store_acc_row<T, FMT>(lane_base + Cfg::kDK + part * kCols, dk + orow + part * kCols, kCols, sm_scale,
+    } else {
+      store_acc_row<T, FMT>(lane_base + Cfg::kDK + cpart * kCols, dk + orow + cpart * kCols, kCols, sm_scale,
                             !have, write);
+    }
   }
 
   tc_fence_before();
@@ -1052,6 +1088,31 @@ bwd_dq_gemm_sm100_kernel(const uint8_t* __restrict__ ds_buf, const __grid_consta
   }
 }
 
+// dK, dV = the sum over head parts of the f32 partials (fixed order), cast to T.
+template <typename T>
+__global__ void dkv_part_reduce_kernel(const float* __restrict__ part, T* __restrict__ dk, T* __restrict__ dv,
+                                       long n4, int parts) {
+  const long n = n4 * 4;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < 2 * n4; i += (long)gridDim.x * blockDim.x) {
+    const bool is_k = i >= n4;
+    const long j = (is_k ? i - n4 : i) * 4;
+    const float* src = part + (is_k ? (long)parts * n : 0) + j;
+    float4 acc = *reinterpret_cast<const float4*>(src);
+    for (int p = 1; p < parts; ++p) {
+      const float4 v = *reinterpret_cast<const float4*>(src + (long)p * n);
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
+    }
+    T* dst = (is_k ? dk : dv) + j;
+    dst[0] = from_f<T>(acc.x);
+    dst[1] = from_f<T>(acc.y);
+    dst[2] = from_f<T>(acc.z);
+    dst[3] = from_f<T>(acc.w);
+  }
+}
+
 template <typename T, int D>
 cudaError_t launch_dkv_t(const BwdArgs& a) {
   using Cfg = DkvCfg<D>;
@@ -1063,14 +1124,21 @@ cudaError_t launch_dkv_t(const BwdArgs& a) {
       !make_tile_map(&tdo, a.dout, a.dtype, D, a.Sq, a.Sq, BH, 128))
     return cudaErrorInvalidValue;
   if (a.ds_buf != nullptr && (reinterpret_cast<uintptr_t>(a.ds_buf) & 15)) return cudaErrorInvalidValue;
+  const int parts = a.dkv_part != nullptr ? a.head_parts : 1;
+  if (parts < 1 || (a.H / a.Hkv) % parts != 0 || (reinterpret_cast<uintptr_t>(a.dkv_part) & 15))
+    return cudaErrorInvalidValue;
   auto kern = bwd_dkv_sm100_kernel<T, D>;
   cudaError_t e = ensure_smem(kern, Cfg::kSmem);
   if (e != cudaSuccess) return e;
   const int n_kt = (a.Sk + 127) / 128;
-  kern<<<n_kt * BHk, EwDkv::kThreads, Cfg::kSmem, a.stream>>>(tk, tv, tq, tdo, reinterpret_cast<uint8_t*>(a.ds_buf),
-                                                       a.lse, a.delta, (T*)a.dk, (T*)a.dv, a.H, a.Hkv, a.Sq,
-                                                       a.Sk, a.kv_len, a.causal, a.sm_scale, a.sm_scale * kLog2e,
-                                                       n_kt);
+  kern<<<n_kt * BHk * parts, EwDkv::kThreads, Cfg::kSmem, a.stream>>>(
+      tk, tv, tq, tdo, reinterpret_cast<uint8_t*>(a.ds_buf), a.dkv_part, parts, a.lse, a.delta, (T*)a.dk, (T*)a.dv,
+      a.H, a.Hkv, a.Sq, a.Sk, a.kv_len, a.causal, a.sm_scale, a.sm_scale * kLog2e, n_kt);
+  e = cudaGetLastError();
+  if (e != cudaSuccess || parts == 1) return e;
+  const long n4 = (long)BHk * a.Sk * D / 4;
+  const long blocks = std::min((2 * n4 + 255) / 256, (long)sm_count() * 8);
+  dkv_part_reduce_kernel<T><<<(unsigned)blocks, 256, 0, a.stream>>>(a.dkv_part, (T*)a.dk, (T*)a.dv, n4, parts);
   return cudaGetLastError();
 }
 
@@ -1115,6 +1183,19 @@ cudaError_t launch_dq_gemm_t(const BwdArgs& a) {
 }
 
 }  // namespace
+
+int bwd_dkv_head_parts(int B, int H, int Hkv, int Sk) {
+  if (B <= 0 || H <= 0 || Hkv <= 0 || H % Hkv != 0 || Sk <= 0) return 1;
+  const int G = H / Hkv;
+  const long ctas = (long)((Sk + 127) / 128) * B * Hkv;
+  int parts = 1;
+  while (G % (parts * 2) == 0 && ctas * parts < sm_count()) parts *= 2;
+  return parts;
+}
+
+size_t bwd_dkv_part_bytes(int B, int Hkv, int Sk, int D, int parts) {
+  return parts > 1 ? (size_t)2 * parts * B * Hkv * Sk * D * sizeof(float) : 0;
+}
 
 size_t bwd_ds_spill_bytes(int B, int H, int Sq, int kv_len, int causal) {
   return (size_t)B * H * ds_tiles_per_plane((Sq + 127) / 128, kv_len, causal) * (128 * 128 * 2);

@@ -236,8 +236,11 @@ size_t pf_bwd_workspace_size(int dtype, int B, int H, int Hkv, int Sq, int Sk, i
   const size_t delta = bwd_delta_bytes(B, H, Sq);
   if (!bwd_sm100_supported(dtype, D)) return delta;
   if (kv_len <= 0 || kv_len > Sk) kv_len = Sk;
-  return delta + bwd_ds_spill_bytes(B, H, Sq, kv_len, causal != 0);
+  return delta + bwd_ds_spill_bytes(B, H, Sq, kv_len, causal != 0) +
+         bwd_dkv_part_bytes(B, Hkv, Sk, D, bwd_dkv_head_parts(B, H, Hkv, Sk));
 }
+
+int pf_bwd_head_parts(int B, int H, int Hkv, int Sk) { return bwd_dkv_head_parts(B, H, Hkv, Sk); }
 
 int pf_bwd(const void* q, const void* k, const void* v, const void* o, const void* dout,
            const float* lse, void* dq, void* dk, void* dv, int dtype, int B, int H, int Hkv,
@@ -265,6 +268,14 @@ int pf_bwd(const void* q, const void* k, const void* v, const void* o, const voi
     const size_t spill = bwd_ds_spill_bytes(B, H, Sq, kv_len, a.causal);
     if (workspace_bytes >= need + spill) {
       a.ds_buf = reinterpret_cast<uint16_t*>(static_cast<uint8_t*>(workspace) + need);
+      // Small problems (fewer key-tile CTAs than SMs): split each kv group's q heads over
+      // several CTAs when the workspace also holds their f32 partial dK/dV.
+      const int parts = bwd_dkv_head_parts(B, H, Hkv, Sk);
+      const size_t part_bytes = bwd_dkv_part_bytes(B, Hkv, Sk, D, parts);
+      if (parts > 1 && workspace_bytes >= need + spill + part_bytes) {
+        a.dkv_part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + need + spill);
+        a.head_parts = parts;
+      }
       // Measured and dropped: chunking the units and overlapping each chunk's dQ
       // GEMM (side stream, small grid) with the next chunk's dK/dV -- a chunk of
       // dK/dV CTAs is bound by its heaviest key tile, so the chunks' tails cost

@@ -36,6 +36,8 @@ struct BwdArgs {
   float* dq_accum;  // f32 [B,H,Sq,D] scratch (tensor-core path)
   uint16_t* ds_buf;  // dS spill of the dK/dV kernel for the dQ GEMM (null: not written)
   int dq_ctas;       // CTAs of the persistent dQ GEMM (0: one per SM)
+  float* dkv_part;   // head-split f32 partial dK/dV (null: no split)
+  int head_parts;    // q-head parts per key tile when dkv_part is set
   cudaStream_t stream;
 };
 
@@ -78,6 +80,11 @@ bool bwd_sm100_supported(int dtype, int D);
 cudaError_t launch_bwd_dkv_sm100(const BwdArgs& a);
 // Bytes of the dS spill (16-bit 128 x 128 tiles of every live key/query tile pair).
 size_t bwd_ds_spill_bytes(int B, int H, int Sq, int kv_len, int causal);
+// q-head parts per key tile of the tensor-core dK/dV kernel (1: no split):
+// doubled while the grid has fewer CTAs than SMs and the group divides.
+int bwd_dkv_head_parts(int B, int H, int Hkv, int Sk);
+// f32 partial dK/dV bytes of a head split into `parts` (0 when parts == 1).
+size_t bwd_dkv_part_bytes(int B, int Hkv, int Sk, int D, int parts);
 // dQ as one GEMM over the spilled dS tiles (after launch_bwd_dkv_sm100 with ds_buf set).
 cudaError_t launch_bwd_dq_gemm_sm100(const BwdArgs& a);
 cudaError_t launch_bwd_dq_sm100(const BwdArgs& a);

@@ -56,6 +56,7 @@ _SIGNATURES = {
     "pf_decode_positions": (_I, [_P, _I, _P, _P, _P, _I, _P]),
     "pf_argmax_embed": (_I, [_P, _L, _I, _I, _P, _P, _P, _I, _I, _P]),
     "pf_bwd_preprocess": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _P]),
+    "pf_bwd_head_parts": (_I, [_I, _I, _I, _I]),
     "pf_bwd_dq": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _F, _I, _P]),
     "pf_bwd_dkv": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _F, _I, _P]),
     "pf_bwd_workspace_size": (_Z, [_I, _I, _I, _I, _I, _I, _I, _I, _I]),
