@@ -36,6 +36,9 @@
  *                       inverse, for the gradient of the RoPE-fused attention)
  *   pf_add_rms_norm     src/pallas_flash/model.py:34-38 (rms_norm) + the residual add before it
  *   pf_silu_mul         src/pallas_flash/model.py:70-74 (the silu(gate) * up of swiglu_mlp)
+ *   pf_rows_linear      src/pallas_flash/model.py:90-101, 120-124, 70-74, 307-356 (a decode
+ *                       step's x @ W projections with the rms_norm before them, the residual
+ *                       add after them, or the SwiGLU activation between them)
  *   pf_decode_positions src/pallas_flash/model.py:434-449, 475-476 (slot, kv_len and RoPE row
  *                       of a decode step, computed on the device)
  *   pf_argmax_embed     src/pallas_flash/model.py:377-383, 520-528 (greedy argmax) + :333, 478
@@ -314,6 +317,25 @@ int pf_add_rms_norm(const void* x, const void* residual, const void* weight,
                     void* stream);
 int pf_silu_mul(const void* gate, const void* up, void* out, int dtype, long rows,
                 int cols, long in_stride, void* stream);
+/* pf_rows_linear: y = epilogue(prologue(x) @ W) for 1 <= M <= 16 rows (a
+ *   decode step's batch), bf16 or f16.  x is [M, K] (16-byte aligned, K a
+ *   multiple of 32, at most 2048); W is passed transposed, wt = W^T [N_w, K]
+ *   row-major.  Prologue: when norm_weight ([K]) is not NULL each row is
+ *   replaced by round((x * rsqrt(mean(x^2) + eps)) * norm_weight), the output
+ *   of pf_add_rms_norm without a residual.  Epilogue by `mode`:
+ *     0: y[M, N] = round(x W)                                  (N_w = N)
+ *     1: y[M, N] = round(residual + round(x W)); residual [M, N] may alias y
+ *     2: y[M, N] = round(round(silu(round(g))) * round(u)) with g = x W[:, :N],
+ *        u = x W[:, N:2N] (N_w = 2N) -- pf_silu_mul of the fused projection.
+ *   N must be a multiple of 32 (16 in mode 2).  fp32 accumulation; the sum
+ *   over K is done in a fixed order (deterministic).  Replaces the matmul and
+ *   its neighbouring pf_add_rms_norm / pf_silu_mul launches of a decode step
+ *   (src/pallas_flash/model.py:90-101, 120-124, 70-74 as called by
+ *   decode_step, :307-356).  PF_ERR_UNSUPPORTED outside those shapes.
+ */
+int pf_rows_linear(const void* x, const void* norm_weight, float eps, const void* wt,
+                   const void* residual, void* y, int dtype, int M, int K, int N, int mode,
+                   void* stream);
 int pf_decode_positions(int64_t* pos, int capacity, int32_t* slots, int32_t* lens,
                         int32_t* rope_rows, int B, void* stream);
 /* pf_argmax_embed: the end of a greedy decode step.  For each of `rows` rows of

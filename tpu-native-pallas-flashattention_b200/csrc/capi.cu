@@ -429,6 +429,23 @@ int pf_add_rms_norm(const void* x, const void* residual, const void* weight, voi
                      "pf_add_rms_norm");
 }
 
+int pf_rows_linear(const void* x, const void* norm_weight, float eps, const void* wt, const void* residual,
+                   void* y, int dtype, int M, int K, int N, int mode, void* stream) {
+  if (!valid_dtype(dtype) || !x || !wt || !y || (mode == 1 && !residual))
+    return fail(PF_ERR_INVALID, "pf_rows_linear: bad argument");
+  if (!(eps >= 0.f)) return fail(PF_ERR_INVALID, "pf_rows_linear: eps must be >= 0");
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(wt) | reinterpret_cast<uintptr_t>(norm_weight)) & 15u)
+    return fail(PF_ERR_INVALID, "pf_rows_linear: x, wt and norm_weight must be 16-byte aligned");
+  if (!rows_linear_supported(dtype, M, K, N, mode))
+    return fail(PF_ERR_UNSUPPORTED,
+                "pf_rows_linear: needs bf16/f16, 1 <= M <= 16, K a multiple of 32 up to 2048, N a multiple of %d, "
+                "mode 0-2 (got dtype %d, M %d, K %d, N %d, mode %d)",
+                mode == 2 ? 16 : 32, dtype, M, K, N, mode);
+  return cuda_status(launch_rows_linear(x, norm_weight, eps, wt, residual, y, dtype, M, K, N, mode,
+                                        static_cast<cudaStream_t>(stream)),
+                     "pf_rows_linear");
+}
+
 int pf_silu_mul(const void* gate, const void* up, void* out, int dtype, long rows, int cols, long in_stride,
                 void* stream) {
   if (!valid_dtype(dtype) || !gate || !up || !out) return fail(PF_ERR_INVALID, "pf_silu_mul: bad argument");

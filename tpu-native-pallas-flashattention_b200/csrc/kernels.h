@@ -109,6 +109,12 @@ cudaError_t launch_add_rms_norm(const void* x, const void* res, const void* w, v
                                 long rows, int dim, float eps, cudaStream_t st);
 cudaError_t launch_silu_mul(const void* g, const void* u, void* out, int dtype, long rows, int cols, long in_stride,
                             cudaStream_t st);
+// Projection of <= 16 rows with an optional RMSNorm prologue and a plain /
+// residual-add / SwiGLU epilogue (rows_linear.cu).
+bool rows_linear_supported(int dtype, int M, int K, int N, int mode);
+size_t rows_linear_smem(int K);
+cudaError_t launch_rows_linear(const void* x, const void* norm_w, float eps, const void* wt, const void* res, void* y,
+                               int dtype, int M, int K, int N, int mode, cudaStream_t st);
 cudaError_t launch_argmax_embed(const void* logits, long row_stride, int vocab, int rows, int64_t* token,
                                 const void* embed, void* x, int dim, int dtype, cudaStream_t st);
 cudaError_t launch_decode_positions(int64_t* pos, int C, int32_t* slots, int32_t* lens, int32_t* rope_rows, int B,

@@ -53,6 +53,7 @@ _SIGNATURES = {
     "pf_rope_fwd": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _P, _I, _I, _I, _I, _I, _I, _I, _I, _F, _I, _P, _Z, _P]),
     "pf_add_rms_norm": (_I, [_P, _P, _P, _P, _P, _I, _L, _I, _F, _P]),
     "pf_silu_mul": (_I, [_P, _P, _P, _I, _L, _I, _L, _P]),
+    "pf_rows_linear": (_I, [_P, _P, _F, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
     "pf_decode_positions": (_I, [_P, _I, _P, _P, _P, _I, _P]),
     "pf_argmax_embed": (_I, [_P, _L, _I, _I, _P, _P, _P, _I, _I, _P]),
     "pf_bwd_preprocess": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _P]),

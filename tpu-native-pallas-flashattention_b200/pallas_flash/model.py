@@ -4,9 +4,13 @@ Drop-in for ``src/pallas_flash/model.py`` of the reference: the same functions,
 parameter pytree (a dict with ``embed``, ``layers`` [list of dicts],
 ``final_norm``, ``lm_head``) and greedy generation loops, on CUDA tensors.
 Attention goes through this package's kernels (``flash_attention`` for
-prefill/forward, ``flash_attention_decode`` for decode steps); the dense layers
-(projections, SwiGLU, lm_head) are plain PyTorch matmuls (cuBLAS), which the
-reference likewise leaves to its compiler.
+prefill/forward, ``flash_attention_decode`` for decode steps).  The dense layers
+(projections, SwiGLU, lm_head) of the prefill and of the lm_head are PyTorch
+matmuls (cuBLAS), which the reference likewise leaves to its compiler; in a
+16-bit decode step of at most 16 sequences the four per-block projections run
+through ``pf_rows_linear`` with the RMSNorm before them, the residual add after
+them and the SwiGLU activation between them folded in (4 launches per block
+where the unfused chain takes 8).
 
 Differences that keep behaviour but suit the GPU:
 * KV caches are preallocated and written **in place** by the cache-write
@@ -215,6 +219,57 @@ def swiglu_mlp(x, w_gate, w_up, w_down):
     return silu_mul(x @ _fused_columns(w_gate, w_up)) @ w_down
 
 
+_FUSED_T: Dict[tuple, tuple] = {}
+
+
+def _fused_rows(*ws: torch.Tensor) -> torch.Tensor:
+    """``[W_1 | W_2 | ...]^T`` as a contiguous ``[out_features, in_features]`` tensor, the
+    weight layout of ``pf_rows_linear``; built once per set of weights (and rebuilt when
+    one of them is modified in place)."""
+    key = tuple(id(w) for w in ws)
+    hit = _FUSED_T.get(key)
+    if hit is not None:
+        refs, versions, fused = hit
+        if all(r() is w for r, w in zip(refs, ws)) and versions == tuple(w._version for w in ws):
+            return fused
+    if len(_FUSED_T) > 512:
+        for k in [k for k, (refs, _, _) in _FUSED_T.items() if any(r() is None for r in refs)]:
+            del _FUSED_T[k]
+    with torch.no_grad():
+        fused = torch.cat(ws, dim=1).t().contiguous()
+    _FUSED_T[key] = (tuple(weakref.ref(w) for w in ws), tuple(w._version for w in ws), fused)
+    return fused
+
+
+def _rows_linear(x: torch.Tensor, wt: torch.Tensor, mode: int, norm: Optional[torch.Tensor] = None,
+                 eps: float = 0.0, residual: Optional[torch.Tensor] = None,
+                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``pf_rows_linear`` on ``x`` [M <= 16, K]: mode 0 ``norm?(x) @ W``, 1 ``residual + x @ W``,
+    2 ``silu(norm?(x) @ W_gate) * (norm?(x) @ W_up)`` with ``wt = [W_gate | W_up]^T``."""
+    M, K = x.shape
+    N = wt.shape[0] // (2 if mode == 2 else 1)
+    y = out if out is not None else torch.empty((M, N), dtype=x.dtype, device=x.device)
+    _lib.check(_lib.lib().pf_rows_linear(
+        x.data_ptr(), _lib.ptr(norm), float(eps), wt.data_ptr(), _lib.ptr(residual), y.data_ptr(),
+        _lib.dtype_code(x.dtype), M, K, N, mode, _lib.stream_of(x)))
+    return y
+
+
+def _fused_decode_ok(params: Params, cfg: ModelConfig, batch: int, dtype) -> bool:
+    """Whether a decode step can run its projections through ``pf_rows_linear`` (16-bit
+    weights, at most 16 rows, dimensions its tiles divide).  The eager step and the graph
+    step take the same choice, so their tokens stay identical."""
+    if dtype not in (torch.bfloat16, torch.float16) or not 1 <= batch <= 16:
+        return False
+    if torch.is_grad_enabled() and any(t.requires_grad for t in (params["embed"], params["lm_head"])):
+        return False
+    width = (cfg.n_heads + 2 * cfg.n_kv_heads) * cfg.head_dim
+    fits = lambda k: k % 32 == 0 and 32 <= k <= 2048  # noqa: E731
+    return (fits(cfg.dim) and fits(cfg.ffn_hidden) and width % 32 == 0 and cfg.dim % 32 == 0
+            and cfg.ffn_hidden % 16 == 0 and cfg.vocab_size % 32 == 0
+            and params["embed"].dtype == dtype and params["lm_head"].dtype == dtype)
+
+
 _ROPE_CACHE: Dict[tuple, tuple] = {}
 
 
@@ -392,6 +447,23 @@ def _decode_layers(params: Params, token, cache: Cache, pos: int, slot: int, kv_
     table = torch.arange(batch, dtype=torch.int32, device=x.device).reshape(batch, 1)
     slots = torch.full((batch,), slot, dtype=torch.int32, device=x.device)
     rows = torch.zeros((batch,), dtype=torch.int32, device=x.device)
+    if _fused_decode_ok(params, cfg, batch, x.dtype):
+        # Projections with their norm / residual add / activation folded in:
+        # 4 launches per block besides RoPE + cache write and attention.
+        xw = x.reshape(batch, cfg.dim)  # the residual stream, updated in place
+        eps = cfg.rms_norm_eps
+        for layer, layer_cache in zip(params["layers"], cache):
+            qkv = _rows_linear(xw, _fused_rows(layer["wq"], layer["wk"], layer["wv"]), 0, norm=layer["attn_norm"],
+                               eps=eps)
+            q = rope_write_to_paged_cache_qkv(qkv.reshape(batch, 1, -1), cfg.n_heads, layer_cache["k"],
+                                              layer_cache["v"], cos, sin, table, slots, rows)
+            attn = flash_attention_decode(q, layer_cache["k"], layer_cache["v"], kv_len, block_k=cfg.block_k)
+            _rows_linear(attn.reshape(batch, cfg.dim), _fused_rows(layer["wo"]), 1, residual=xw, out=xw)
+            act = _rows_linear(xw, _fused_rows(layer["w_gate"], layer["w_up"]), 2, norm=layer["ffn_norm"], eps=eps)
+            _rows_linear(act, _fused_rows(layer["w_down"]), 1, residual=xw, out=xw)
+        # the final norm and lm_head (32000 columns) stay on the norm kernel + library matmul
+        _, h = add_rms_norm(x, None, params["final_norm"], eps)
+        return h @ params["lm_head"], cache
     mlp = None  # each block's MLP output is added by the next norm's launch
     for layer, layer_cache in zip(params["layers"], cache):
         x, h = add_rms_norm(x, mlp, layer["attn_norm"], cfg.rms_norm_eps)
@@ -456,6 +528,35 @@ class DecodeGraph:
                                                   self.slots.numel(), _lib.stream_of(self.pos)))
         x = self.x
         batch = x.shape[0]
+        if _fused_decode_ok(p, cfg, batch, x.dtype):
+            # as _decode_layers: the residual stream is self.x, updated in place (the
+            # argmax + embedding kernel writes the next step's rows over it at the end)
+            xw = x.view(batch, cfg.dim)
+            eps = cfg.rms_norm_eps
+            for layer, lc in zip(p["layers"], self.cache):
+                qkv = _rows_linear(xw, _fused_rows(layer["wq"], layer["wk"], layer["wv"]), 0,
+                                   norm=layer["attn_norm"], eps=eps)
+                q = rope_write_to_paged_cache_qkv(qkv.reshape(batch, 1, -1), cfg.n_heads, lc["k"], lc["v"],
+                                                  self.cos, self.sin, self.table, self.slots, self.rope_rows)
+                attn = paged_flash_attention(q, lc["k"], lc["v"], self.table, self.lens, max_context_len=self.C)
+                _rows_linear(attn.reshape(batch, cfg.dim), _fused_rows(layer["wo"]), 1, residual=xw, out=xw)
+                act = _rows_linear(xw, _fused_rows(layer["w_gate"], layer["w_up"]), 2, norm=layer["ffn_norm"],
+                                   eps=eps)
+                _rows_linear(act, _fused_rows(layer["w_down"]), 1, residual=xw, out=xw)
+            _, h = add_rms_norm(x, None, p["final_norm"], eps)
+            logits = (h @ p["lm_head"]).reshape(batch, -1)
+        else:
+            logits = self._step_unfused(x, batch)
+        embed = p["embed"].contiguous()
+        if embed.dtype != logits.dtype:
+            raise ValueError("the embedding table and lm_head must share a dtype for the graph decode step")
+        # greedy token (first maximum, as torch.argmax) and the next step's embedding row
+        _lib.check(_lib.lib().pf_argmax_embed(logits.data_ptr(), logits.shape[-1], logits.shape[-1], batch,
+                                              self.token.data_ptr(), embed.data_ptr(), self.x.data_ptr(),
+                                              cfg.dim, _lib.dtype_code(logits.dtype), _lib.stream_of(logits)))
+
+    def _step_unfused(self, x, batch):
+        cfg, p = self.cfg, self.params
         mlp = None
         for layer, lc in zip(p["layers"], self.cache):
             x, h = add_rms_norm(x, mlp, layer["attn_norm"], cfg.rms_norm_eps)
@@ -467,14 +568,7 @@ class DecodeGraph:
                                 layer["ffn_norm"], cfg.rms_norm_eps)
             mlp = swiglu_mlp(h, layer["w_gate"], layer["w_up"], layer["w_down"])
         x, h = add_rms_norm(x, mlp, p["final_norm"], cfg.rms_norm_eps)
-        logits = (h @ p["lm_head"]).contiguous()
-        embed = p["embed"].contiguous()
-        if embed.dtype != logits.dtype:
-            raise ValueError("the embedding table and lm_head must share a dtype for the graph decode step")
-        # greedy token (first maximum, as torch.argmax) and the next step's embedding row
-        _lib.check(_lib.lib().pf_argmax_embed(logits.data_ptr(), logits.shape[-1], logits.shape[-1], batch,
-                                              self.token.data_ptr(), embed.data_ptr(), self.x.data_ptr(),
-                                              cfg.dim, _lib.dtype_code(logits.dtype), _lib.stream_of(logits)))
+        return (h @ p["lm_head"]).reshape(batch, -1).contiguous()
 
     def capture(self, token, pos: int, last_pos: int):
         """One eager warm-up step at ``pos`` (it writes cache slot ``pos`` with the values the
