@@ -39,6 +39,9 @@
  *   pf_rows_linear      src/pallas_flash/model.py:90-101, 120-124, 70-74, 307-356 (a decode
  *                       step's x @ W projections with the rms_norm before them, the residual
  *                       add after them, or the SwiGLU activation between them)
+ *   pf_rows_linear_rope_write  the same step's q/k/v projection (model.py:90-101) with
+ *                       rope (model.py:41-67) and the cache write (model.py:307-356,
+ *                       paged.py:205-223) as its epilogue
  *   pf_decode_positions src/pallas_flash/model.py:434-449, 475-476 (slot, kv_len and RoPE row
  *                       of a decode step, computed on the device)
  *   pf_argmax_embed     src/pallas_flash/model.py:377-383, 520-528 (greedy argmax) + :333, 478
@@ -336,6 +339,24 @@ int pf_silu_mul(const void* gate, const void* up, void* out, int dtype, long row
 int pf_rows_linear(const void* x, const void* norm_weight, float eps, const void* wt,
                    const void* residual, void* y, int dtype, int M, int K, int N, int mode,
                    void* stream);
+/* pf_rows_linear_rope_write: one decode token per sequence through the fused
+ *   q/k/v projection, RoPE and the K/V cache write, in one launch.  The
+ *   projection is pf_rows_linear mode 0 (M = B rows of x [B, K], optional
+ *   RMSNorm prologue) with wt = [W_q | W_k | W_v]^T [(H + 2*Hkv) * D, K]; its
+ *   rounded output then goes exactly where pf_rope_paged_write_qkv sends a
+ *   [B, (H + 2*Hkv) * D] projection: q heads rotated into q_out [B, H, 1, D],
+ *   k heads rotated and v heads copied into page
+ *   block_tables[b][positions[b] / page_size], row positions[b] % page_size,
+ *   with the RoPE table row rope_positions[b] (clamped to the table).  head_dim
+ *   must be a multiple of 32; other limits as pf_rows_linear.
+ */
+int pf_rows_linear_rope_write(const void* x, const void* norm_weight, float eps, const void* wt,
+                              void* q_out, void* k_pages, void* v_pages, const void* cos_t,
+                              const void* sin_t, int table_dtype, int table_rows,
+                              const int32_t* block_tables, const int32_t* positions,
+                              const int32_t* rope_positions, int dtype, int B, int K, int H,
+                              int Hkv, int num_pages, int page_size, int pages_per_seq, int D,
+                              void* stream);
 int pf_decode_positions(int64_t* pos, int capacity, int32_t* slots, int32_t* lens,
                         int32_t* rope_rows, int B, void* stream);
 /* pf_argmax_embed: the end of a greedy decode step.  For each of `rows` rows of

@@ -128,3 +128,38 @@ def test_decode_step_fused_projections_match_unfused_logits():
     err = (fused.float() - unfused.float()).abs().max().item()
     scale = unfused.float().abs().amax().item()
     assert err <= 0.03 * scale, (err, scale)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("B,H,Hkv,D,page_size", [(16, 8, 2, 64, 512), (3, 4, 4, 128, 16), (1, 2, 1, 32, 8)])
+def test_rows_linear_rope_write_equals_projection_then_rope_write(dtype, B, H, Hkv, D, page_size):
+    """One launch (projection + RoPE + cache write) == pf_rows_linear followed by
+    pf_rope_paged_write_qkv on its output: the same rounded projection goes through the
+    same rotation arithmetic, so q and both pools must be bit-identical."""
+    g = torch.Generator(device="cuda").manual_seed(B * 7 + D)
+    K = 512
+    width = (H + 2 * Hkv) * D
+    x = torch.randn((B, K), device="cuda", generator=g).to(dtype)
+    wt = (torch.randn((width, K), device="cuda", generator=g) / K ** 0.5).to(dtype)
+    norm = (1.0 + 0.1 * torch.randn((K,), device="cuda", generator=g)).to(dtype)
+    pps = 4
+    num_pages = B * pps + 3
+    cos, sin = pf.precompute_rope(300, D, 10000.0, device="cuda")
+    table = torch.randperm(num_pages, device="cuda", generator=g)[:B * pps].to(torch.int32).reshape(B, pps)
+    pos = torch.randint(0, pps * page_size, (B,), device="cuda", generator=g).to(torch.int32)
+    rpos = torch.randint(0, 300, (B,), device="cuda", generator=g).to(torch.int32)
+    pools = [torch.randn((num_pages, Hkv, page_size, D), device="cuda", generator=g).to(dtype) for _ in range(2)]
+    ka, va = pools[0].clone(), pools[1].clone()
+    kb, vb = pools[0].clone(), pools[1].clone()
+    qa = torch.empty((B, H, 1, D), device="cuda", dtype=dtype)
+    L = _lib.lib()
+    _lib.check(L.pf_rows_linear_rope_write(
+        x.data_ptr(), norm.data_ptr(), 1e-5, wt.data_ptr(), qa.data_ptr(), ka.data_ptr(), va.data_ptr(),
+        cos.data_ptr(), sin.data_ptr(), _lib.dtype_code(cos.dtype), cos.shape[0], table.data_ptr(), pos.data_ptr(),
+        rpos.data_ptr(), _lib.dtype_code(dtype), B, K, H, Hkv, num_pages, page_size, pps, D, None))
+    qkv = run(x, wt, 0, norm=norm)
+    qb = pf.rope_write_to_paged_cache_qkv(qkv.reshape(B, 1, width), H, kb, vb, cos, sin, table, pos, rpos)
+    torch.cuda.synchronize()
+    assert torch.equal(qa, qb)
+    assert torch.equal(ka, kb) and torch.equal(va, vb)
+    assert not torch.equal(ka, pools[0])  # the rows were written

@@ -118,8 +118,8 @@ __device__ __forceinline__ void rope_row_in_smem(uint8_t* tile, int row, const v
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
       const float a = to_f(x0[u]), bb = to_f(x1[u]);
-      x0[u] = from_f<T>(a * c0[buf][u] - bb * s0[buf][u]);
-      x1[u] = from_f<T>(bb * c1[buf][u] + a * s1[buf][u]);
+      x0[u] = from_f<T>(rope_lo(a, bb, c0[buf][u], s0[buf][u]));
+      x1[u] = from_f<T>(rope_hi(a, bb, c1[buf][u], s1[buf][u]));
     }
     *p0 = v0;
     *p1 = v1;
@@ -647,8 +647,8 @@ __global__ void rope_rows_kernel(const T* __restrict__ x, T* __restrict__ out, c
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
       const float a = to_f(x0[u]), bb = to_f(x1[u]);
-      x0[u] = from_f<T>(a * c0[u] - bb * s0[u]);
-      x1[u] = from_f<T>(bb * c1[u] + a * s1[u]);
+      x0[u] = from_f<T>(rope_lo(a, bb, c0[u], s0[u]));
+      x1[u] = from_f<T>(rope_hi(a, bb, c1[u], s1[u]));
     }
     *reinterpret_cast<uint4*>(out + base + d0) = v0;
     *reinterpret_cast<uint4*>(out + base + d1) = v1;

@@ -446,6 +446,33 @@ int pf_rows_linear(const void* x, const void* norm_weight, float eps, const void
                      "pf_rows_linear");
 }
 
+int pf_rows_linear_rope_write(const void* x, const void* norm_weight, float eps, const void* wt, void* q_out,
+                              void* k_pages, void* v_pages, const void* cos_t, const void* sin_t, int table_dtype,
+                              int table_rows, const int32_t* block_tables, const int32_t* positions,
+                              const int32_t* rope_positions, int dtype, int B, int K, int H, int Hkv, int num_pages,
+                              int page_size, int pages_per_seq, int D, void* stream) {
+  const char* fn = "pf_rows_linear_rope_write";
+  if (!valid_dtype(dtype) || !valid_dtype(table_dtype) || !x || !wt || !q_out || !k_pages || !v_pages || !cos_t ||
+      !sin_t || !block_tables || !positions || !rope_positions)
+    return fail(PF_ERR_INVALID, "%s: bad argument", fn);
+  if (!(eps >= 0.f)) return fail(PF_ERR_INVALID, "%s: eps must be >= 0", fn);
+  if (B <= 0 || H <= 0 || Hkv <= 0 || num_pages <= 0 || page_size <= 0 || pages_per_seq <= 0 || D <= 0 ||
+      table_rows <= 0)
+    return fail(PF_ERR_INVALID, "%s: shapes must be positive", fn);
+  if (H % Hkv != 0) return fail(PF_ERR_INVALID, "%s: num_heads must be a multiple of num_kv_heads", fn);
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(wt) | reinterpret_cast<uintptr_t>(norm_weight)) & 15u)
+    return fail(PF_ERR_INVALID, "%s: x, wt and norm_weight must be 16-byte aligned", fn);
+  if (!rows_linear_rope_supported(dtype, B, K, H, Hkv, D))
+    return fail(PF_ERR_UNSUPPORTED,
+                "%s: needs bf16/f16, 1 <= B <= 16, K a multiple of 32 up to 2048, head_dim a multiple of 32 "
+                "(got dtype %d, B %d, K %d, head_dim %d)", fn, dtype, B, K, D);
+  return cuda_status(launch_rows_linear_rope_write(x, norm_weight, eps, wt, q_out, k_pages, v_pages, cos_t, sin_t,
+                                                   table_dtype, table_rows, block_tables, positions, rope_positions,
+                                                   dtype, B, K, H, Hkv, num_pages, page_size, pages_per_seq, D,
+                                                   static_cast<cudaStream_t>(stream)),
+                     fn);
+}
+
 int pf_silu_mul(const void* gate, const void* up, void* out, int dtype, long rows, int cols, long in_stride,
                 void* stream) {
   if (!valid_dtype(dtype) || !gate || !up || !out) return fail(PF_ERR_INVALID, "pf_silu_mul: bad argument");

@@ -32,6 +32,16 @@ template <typename T> __device__ __forceinline__ float to_f(T x) { return Elem<T
 template <typename T> __device__ __forceinline__ T from_f(float x) { return Elem<T>::from_f(x); }
 
 // Reads element i of a table whose dtype is only known at run time.
+// The two halves of a RoPE rotation, x1 * c1 - x2 * s1 and x2 * c2 + x1 * s2,
+// with every product and sum rounded separately (no FMA contraction), so every
+// kernel that rotates a row produces the same bits.
+__device__ __forceinline__ float rope_lo(float x1, float x2, float c1, float s1) {
+  return __fsub_rn(__fmul_rn(x1, c1), __fmul_rn(x2, s1));
+}
+__device__ __forceinline__ float rope_hi(float x1, float x2, float c2, float s2) {
+  return __fadd_rn(__fmul_rn(x2, c2), __fmul_rn(x1, s2));
+}
+
 __device__ __forceinline__ float load_any(const void* p, int dtype, long i) {
   if (dtype == PF_F32) return static_cast<const float*>(p)[i];
   if (dtype == PF_BF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);

@@ -363,8 +363,8 @@ __global__ void rope_paged_write_kernel(const T* q_in, long q_bs, T* q_out, T* k
     const T* x = q_in + (long)b * q_bs + (long)head * D;
     T* y = q_out + ((long)b * H + head) * D;
     const float x1 = to_f(x[i]), x2 = to_f(x[i + half]);
-    y[i] = from_f<T>(x1 * c1 - x2 * s1);
-    y[i + half] = from_f<T>(x2 * c2 + x1 * s2);
+    y[i] = from_f<T>(rope_lo(x1, x2, c1, s1));
+    y[i + half] = from_f<T>(rope_hi(x1, x2, c2, s2));
     return;
   }
   const int hk = head - H;
@@ -376,8 +376,8 @@ __global__ void rope_paged_write_kernel(const T* q_in, long q_bs, T* q_out, T* k
   const long dst = (((long)page * Hkv + hk) * ps + off) * D;
   const long src = (long)b * kv_bs + (long)hk * D;
   const float x1 = to_f(k[src + i]), x2 = to_f(k[src + i + half]);
-  kp[dst + i] = from_f<T>(x1 * c1 - x2 * s1);
-  kp[dst + i + half] = from_f<T>(x2 * c2 + x1 * s2);
+  kp[dst + i] = from_f<T>(rope_lo(x1, x2, c1, s1));
+  kp[dst + i + half] = from_f<T>(rope_hi(x1, x2, c2, s2));
   vp[dst + i] = v[src + i];
   vp[dst + i + half] = v[src + i + half];
 }

@@ -115,6 +115,13 @@ bool rows_linear_supported(int dtype, int M, int K, int N, int mode);
 size_t rows_linear_smem(int K);
 cudaError_t launch_rows_linear(const void* x, const void* norm_w, float eps, const void* wt, const void* res, void* y,
                                int dtype, int M, int K, int N, int mode, cudaStream_t st);
+bool rows_linear_rope_supported(int dtype, int M, int K, int H, int Hkv, int D);
+cudaError_t launch_rows_linear_rope_write(const void* x, const void* norm_w, float eps, const void* wt, void* q_out,
+                                          void* k_pages, void* v_pages, const void* cos_t, const void* sin_t,
+                                          int tdtype, int table_rows, const int32_t* tables,
+                                          const int32_t* positions, const int32_t* rope_pos, int dtype, int M, int K,
+                                          int H, int Hkv, int num_pages, int page_size, int pages_per_seq, int D,
+                                          cudaStream_t st);
 cudaError_t launch_argmax_embed(const void* logits, long row_stride, int vocab, int rows, int64_t* token,
                                 const void* embed, void* x, int dim, int dtype, cudaStream_t st);
 cudaError_t launch_decode_positions(int64_t* pos, int C, int32_t* slots, int32_t* lens, int32_t* rope_rows, int B,

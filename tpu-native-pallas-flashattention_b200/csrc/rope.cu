@@ -27,8 +27,8 @@ __global__ void rope_apply_kernel(const T* __restrict__ x, const void* __restric
     const float c1 = load_any(cos_t, tdtype, s * D + i), s1 = sgn * load_any(sin_t, tdtype, s * D + i);
     const float c2 = load_any(cos_t, tdtype, s * D + i + half);
     const float s2 = sgn * load_any(sin_t, tdtype, s * D + i + half);
-    out[base + i] = from_f<T>(x1 * c1 - x2 * s1);
-    out[base + i + half] = from_f<T>(x2 * c2 + x1 * s2);
+    out[base + i] = from_f<T>(rope_lo(x1, x2, c1, s1));
+    out[base + i + half] = from_f<T>(rope_hi(x1, x2, c2, s2));
   }
 }
 

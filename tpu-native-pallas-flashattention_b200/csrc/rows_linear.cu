@@ -35,6 +35,22 @@
 namespace pf {
 namespace {
 
+// Mode 3: the fused q/k/v projection of one decode token per sequence, with
+// RoPE and the K/V cache write as its epilogue (the arithmetic and addressing
+// of rope_paged_write_kernel).  A CTA owns 16 rotation pairs (d, d + D/2) of
+// one head: weight rows [head*D + 16s, +16) and [head*D + D/2 + 16s, +16).
+struct RlRope {
+  void* q_out;             // [M, H, 1, D]
+  void* k_pages;           // [num_pages, Hkv, page_size, D]
+  void* v_pages;
+  const void* cos_t;       // [table_rows, D] (tdtype)
+  const void* sin_t;
+  const int32_t* tables;   // [M, pages_per_seq]
+  const int32_t* positions;  // cache position written, per sequence
+  const int32_t* rope_pos;   // RoPE table row, per sequence
+  int tdtype, table_rows, H, Hkv, num_pages, page_size, pages_per_seq, D;
+};
+
 constexpr int kRlThreads = 256;
 constexpr int kRlWarps = kRlThreads / 32;
 constexpr int kRlCols = 32;     // weight rows (output features) per CTA
@@ -63,7 +79,7 @@ __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], 
 template <typename T, int MAXU>
 __global__ void __launch_bounds__(kRlThreads)
 rows_linear_kernel(const T* __restrict__ x, const T* __restrict__ norm_w, float eps, const T* __restrict__ wt,
-                   const T* res, T* y, int M, int K, int N, int mode) {
+                   const T* res, T* y, int M, int K, int N, int mode, RlRope rp) {
   extern __shared__ __align__(16) uint8_t rl_smem[];
   const int lda = K + 8;  // row stride of the A tile in elements (16 B of padding: no bank conflicts)
   T* A = reinterpret_cast<T*>(rl_smem);
@@ -72,10 +88,16 @@ rows_linear_kernel(const T* __restrict__ x, const T* __restrict__ norm_w, float 
   const int g = lane / 4, c = lane % 4;
 
   // Weight rows of this CTA's four 8-row n-tiles.
-  const int cb = blockIdx.x * (mode == 2 ? kRlCols / 2 : kRlCols);
+  const int cb = blockIdx.x * (mode >= 2 ? kRlCols / 2 : kRlCols);
   int wrow[4];
+  if (mode == 3) {
+    const int per_head = rp.D / 32, head = blockIdx.x / per_head, s16 = 16 * (blockIdx.x % per_head);
 #pragma unroll
-  for (int t = 0; t < 4; ++t) wrow[t] = (mode == 2 && t >= 2) ? N + cb + 8 * (t - 2) + g : cb + 8 * t + g;
+    for (int t = 0; t < 4; ++t) wrow[t] = head * rp.D + (t >= 2 ? rp.D / 2 : 0) + s16 + 8 * (t & 1) + g;
+  } else {
+#pragma unroll
+    for (int t = 0; t < 4; ++t) wrow[t] = (mode == 2 && t >= 2) ? N + cb + 8 * (t - 2) + g : cb + 8 * t + g;
+  }
 
   // This warp's K units [u0, u1); every weight load is issued before the prologue.
   const int U = K / 32;
@@ -193,7 +215,40 @@ rows_linear_kernel(const T* __restrict__ x, const T* __restrict__ norm_w, float 
     for (int w = 0; w < kRlWarps; ++w) s += red[(w * 16 + r) * kRlCols + j];
     return s;
   };
-  if (mode == 2) {
+  if (mode == 3) {
+    const int r = threadIdx.x / 16, j = threadIdx.x % 16;  // 16 rows x 16 rotation pairs
+    if (r < M) {
+      const int D = rp.D, half = D / 2, per_head = D / 32;
+      const int head = blockIdx.x / per_head, i = 16 * (blockIdx.x % per_head) + j;
+      const float x1 = to_f(from_f<T>(total(r, j))), x2 = to_f(from_f<T>(total(r, j + 16)));
+      const long tr = min(max(rp.rope_pos[r], 0), rp.table_rows - 1);
+      const float c1 = load_any(rp.cos_t, rp.tdtype, tr * D + i), s1 = load_any(rp.sin_t, rp.tdtype, tr * D + i);
+      const float c2 = load_any(rp.cos_t, rp.tdtype, tr * D + i + half);
+      const float s2 = load_any(rp.sin_t, rp.tdtype, tr * D + i + half);
+      if (head < rp.H) {
+        T* q = static_cast<T*>(rp.q_out) + ((long)r * rp.H + head) * D;
+        q[i] = from_f<T>(rope_lo(x1, x2, c1, s1));
+        q[i + half] = from_f<T>(rope_hi(x1, x2, c2, s2));
+      } else {
+        const int hk = head < rp.H + rp.Hkv ? head - rp.H : head - rp.H - rp.Hkv;
+        const int pos = rp.positions[r], ps = rp.page_size;
+        const int lp = min(max(pos / ps, 0), rp.pages_per_seq - 1);
+        const int off = pos - (pos / ps) * ps;
+        int page = rp.tables[(long)r * rp.pages_per_seq + lp];
+        page = min(max(page, 0), rp.num_pages - 1);
+        const long dst = (((long)page * rp.Hkv + hk) * ps + off) * D;
+        if (head < rp.H + rp.Hkv) {
+          T* kp = static_cast<T*>(rp.k_pages);
+          kp[dst + i] = from_f<T>(rope_lo(x1, x2, c1, s1));
+          kp[dst + i + half] = from_f<T>(rope_hi(x1, x2, c2, s2));
+        } else {
+          T* vp = static_cast<T*>(rp.v_pages);
+          vp[dst + i] = from_f<T>(x1);
+          vp[dst + i + half] = from_f<T>(x2);
+        }
+      }
+    }
+  } else if (mode == 2) {
     const int r = threadIdx.x / 16, j = threadIdx.x % 16;  // 256 threads = 16 rows x 16 columns
     if (r < M) {
       const float gv = to_f(from_f<T>(total(r, j))), uv = to_f(from_f<T>(total(r, j + 16)));
@@ -222,17 +277,21 @@ bool rows_linear_supported(int dtype, int M, int K, int N, int mode) {
   return N > 0 && N % (mode == 2 ? kRlCols / 2 : kRlCols) == 0;
 }
 
-cudaError_t launch_rows_linear(const void* x, const void* norm_w, float eps, const void* wt, const void* res, void* y,
-                               int dtype, int M, int K, int N, int mode, cudaStream_t st) {
+bool rows_linear_rope_supported(int dtype, int M, int K, int H, int Hkv, int D) {
+  return rows_linear_supported(dtype, M, K, 32, 0) && H > 0 && Hkv > 0 && D >= 32 && D % 32 == 0;
+}
+
+static cudaError_t launch_rl(const void* x, const void* norm_w, float eps, const void* wt, const void* res, void* y,
+                             int dtype, int M, int K, int N, int mode, const RlRope& rp, cudaStream_t st) {
   const size_t smem = rows_linear_smem(K);
-  const unsigned grid = (unsigned)(N / (mode == 2 ? kRlCols / 2 : kRlCols));
+  const unsigned grid = (unsigned)(N / (mode >= 2 ? kRlCols / 2 : kRlCols));
 #define PF_RL(T, U)                                                                                              \
   do {                                                                                                           \
     cudaError_t e = ensure_smem(rows_linear_kernel<T, U>, (int)rows_linear_smem(kRlWarps * (U) * 32));         \
     if (e != cudaSuccess) return e;                                                                              \
     rows_linear_kernel<T, U><<<grid, kRlThreads, smem, st>>>(                                                    \
         static_cast<const T*>(x), static_cast<const T*>(norm_w), eps, static_cast<const T*>(wt),                 \
-        static_cast<const T*>(res), static_cast<T*>(y), M, K, N, mode);                                          \
+        static_cast<const T*>(res), static_cast<T*>(y), M, K, N, mode, rp);                                      \
   } while (0)
 #define PF_RL_U(T)                              \
   do {                                          \
@@ -246,6 +305,23 @@ cudaError_t launch_rows_linear(const void* x, const void* norm_w, float eps, con
 #undef PF_RL_U
 #undef PF_RL
   return cudaGetLastError();
+}
+
+cudaError_t launch_rows_linear(const void* x, const void* norm_w, float eps, const void* wt, const void* res, void* y,
+                               int dtype, int M, int K, int N, int mode, cudaStream_t st) {
+  return launch_rl(x, norm_w, eps, wt, res, y, dtype, M, K, N, mode, RlRope{}, st);
+}
+
+cudaError_t launch_rows_linear_rope_write(const void* x, const void* norm_w, float eps, const void* wt, void* q_out,
+                                          void* k_pages, void* v_pages, const void* cos_t, const void* sin_t,
+                                          int tdtype, int table_rows, const int32_t* tables,
+                                          const int32_t* positions, const int32_t* rope_pos, int dtype, int M, int K,
+                                          int H, int Hkv, int num_pages, int page_size, int pages_per_seq, int D,
+                                          cudaStream_t st) {
+  RlRope rp{q_out, k_pages, v_pages, cos_t, sin_t, tables, positions, rope_pos,
+            tdtype, table_rows, H, Hkv, num_pages, page_size, pages_per_seq, D};
+  const int pairs = (H + 2 * Hkv) * D / 2;
+  return launch_rl(x, norm_w, eps, wt, nullptr, nullptr, dtype, M, K, pairs, 3, rp, st);
 }
 
 }  // namespace pf

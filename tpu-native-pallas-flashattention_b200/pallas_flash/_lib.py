@@ -54,6 +54,8 @@ _SIGNATURES = {
     "pf_add_rms_norm": (_I, [_P, _P, _P, _P, _P, _I, _L, _I, _F, _P]),
     "pf_silu_mul": (_I, [_P, _P, _P, _I, _L, _I, _L, _P]),
     "pf_rows_linear": (_I, [_P, _P, _F, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
+    "pf_rows_linear_rope_write": (_I, [_P, _P, _F, _P, _P, _P, _P, _P, _P, _I, _I, _P, _P, _P, _I, _I, _I, _I, _I,
+                                       _I, _I, _I, _I, _P]),
     "pf_decode_positions": (_I, [_P, _I, _P, _P, _P, _I, _P]),
     "pf_argmax_embed": (_I, [_P, _L, _I, _I, _P, _P, _P, _I, _I, _P]),
     "pf_bwd_preprocess": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _P]),

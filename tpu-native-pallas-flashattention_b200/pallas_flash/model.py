@@ -9,8 +9,9 @@ prefill/forward, ``flash_attention_decode`` for decode steps).  The dense layers
 matmuls (cuBLAS), which the reference likewise leaves to its compiler; in a
 16-bit decode step of at most 16 sequences the four per-block projections run
 through ``pf_rows_linear`` with the RMSNorm before them, the residual add after
-them and the SwiGLU activation between them folded in (4 launches per block
-where the unfused chain takes 8).
+them and the SwiGLU activation between them folded in, and RoPE plus the K/V
+cache write in the q/k/v projection's epilogue (5 launches per block with the
+attention, where the unfused chain takes 9).
 
 Differences that keep behaviour but suit the GPU:
 * KV caches are preallocated and written **in place** by the cache-write
@@ -255,6 +256,29 @@ def _rows_linear(x: torch.Tensor, wt: torch.Tensor, mode: int, norm: Optional[to
     return y
 
 
+def _qkv_rope_write(x: torch.Tensor, layer: Params, norm: torch.Tensor, eps: float, cfg: ModelConfig,
+                    k_pages, v_pages, cos, sin, table, slots, rope_rows) -> torch.Tensor:
+    """The normed q/k/v projection of one token per sequence with RoPE and the K/V cache
+    write folded in (``pf_rows_linear_rope_write``, one launch); returns the rotated q
+    ``[batch, n_heads, 1, head_dim]``.  The fixed / ring cache is addressed as a pool of
+    one page per sequence, as ``rope_write_to_paged_cache_qkv`` does."""
+    wt = _fused_rows(layer["wq"], layer["wk"], layer["wv"])
+    if cfg.head_dim % 32 != 0:
+        qkv = _rows_linear(x, wt, 0, norm=norm, eps=eps)
+        return rope_write_to_paged_cache_qkv(qkv.reshape(x.shape[0], 1, -1), cfg.n_heads, k_pages, v_pages, cos,
+                                             sin, table, slots, rope_rows)
+    batch, K = x.shape
+    num_pages, n_kv, page_size, head_dim = k_pages.shape
+    q = torch.empty((batch, cfg.n_heads, 1, head_dim), dtype=x.dtype, device=x.device)
+    sin = sin.to(cos.dtype)
+    _lib.check(_lib.lib().pf_rows_linear_rope_write(
+        x.data_ptr(), norm.data_ptr(), float(eps), wt.data_ptr(), q.data_ptr(), k_pages.data_ptr(),
+        v_pages.data_ptr(), cos.contiguous().data_ptr(), sin.contiguous().data_ptr(), _lib.dtype_code(cos.dtype),
+        cos.shape[0], table.data_ptr(), slots.data_ptr(), rope_rows.data_ptr(), _lib.dtype_code(x.dtype), batch, K,
+        cfg.n_heads, n_kv, num_pages, page_size, table.shape[1], head_dim, _lib.stream_of(x)))
+    return q
+
+
 def _fused_decode_ok(params: Params, cfg: ModelConfig, batch: int, dtype) -> bool:
     """Whether a decode step can run its projections through ``pf_rows_linear`` (16-bit
     weights, at most 16 rows, dimensions its tiles divide).  The eager step and the graph
@@ -453,10 +477,8 @@ def _decode_layers(params: Params, token, cache: Cache, pos: int, slot: int, kv_
         xw = x.reshape(batch, cfg.dim)  # the residual stream, updated in place
         eps = cfg.rms_norm_eps
         for layer, layer_cache in zip(params["layers"], cache):
-            qkv = _rows_linear(xw, _fused_rows(layer["wq"], layer["wk"], layer["wv"]), 0, norm=layer["attn_norm"],
-                               eps=eps)
-            q = rope_write_to_paged_cache_qkv(qkv.reshape(batch, 1, -1), cfg.n_heads, layer_cache["k"],
-                                              layer_cache["v"], cos, sin, table, slots, rows)
+            q = _qkv_rope_write(xw, layer, layer["attn_norm"], eps, cfg, layer_cache["k"], layer_cache["v"], cos, sin,
+                                table, slots, rows)
             attn = flash_attention_decode(q, layer_cache["k"], layer_cache["v"], kv_len, block_k=cfg.block_k)
             _rows_linear(attn.reshape(batch, cfg.dim), _fused_rows(layer["wo"]), 1, residual=xw, out=xw)
             act = _rows_linear(xw, _fused_rows(layer["w_gate"], layer["w_up"]), 2, norm=layer["ffn_norm"], eps=eps)
@@ -534,10 +556,8 @@ class DecodeGraph:
             xw = x.view(batch, cfg.dim)
             eps = cfg.rms_norm_eps
             for layer, lc in zip(p["layers"], self.cache):
-                qkv = _rows_linear(xw, _fused_rows(layer["wq"], layer["wk"], layer["wv"]), 0,
-                                   norm=layer["attn_norm"], eps=eps)
-                q = rope_write_to_paged_cache_qkv(qkv.reshape(batch, 1, -1), cfg.n_heads, lc["k"], lc["v"],
-                                                  self.cos, self.sin, self.table, self.slots, self.rope_rows)
+                q = _qkv_rope_write(xw, layer, layer["attn_norm"], eps, cfg, lc["k"], lc["v"], self.cos, self.sin,
+                                    self.table, self.slots, self.rope_rows)
                 attn = paged_flash_attention(q, lc["k"], lc["v"], self.table, self.lens, max_context_len=self.C)
                 _rows_linear(attn.reshape(batch, cfg.dim), _fused_rows(layer["wo"]), 1, residual=xw, out=xw)
                 act = _rows_linear(xw, _fused_rows(layer["w_gate"], layer["w_up"]), 2, norm=layer["ffn_norm"],
