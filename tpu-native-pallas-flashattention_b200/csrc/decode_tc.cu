@@ -118,6 +118,13 @@ decode_tc_kernel(DecodeArgs a, const __grid_constant__ CUtensorMap tm_k, const _
   const int gcount = min(16, hk * G + G - h0);
   const bool paged = a.block_tables != nullptr;
 
+  // Launched as a programmatic dependent of the previous kernel on the stream
+  // (a decode step's RoPE + cache write): wait for it before reading lengths,
+  // tables, q or the cache, then let the next kernel launch (the output
+  // projection prefetches its weights while this one runs).
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
   int len = a.context_lens ? a.context_lens[b] : a.fixed_len;
   if (paged && len > a.pages_per_seq * a.page_size) {
     if (threadIdx.x == 0) flag_status(PF_DEV_BAD_PAGE);
@@ -408,8 +415,17 @@ cudaError_t launch_tc_kernel(const DecodeArgs& a, const CUtensorMap& tk, const C
   cudaError_t e = ensure_smem(kern, Cfg::kSmem);
   if (e != cudaSuccess) return e;
   dim3 grid(a.num_splits, a.Hkv * head_chunks, a.B);
-  kern<<<grid, kWarps * 32, Cfg::kSmem, a.stream>>>(a, tk, tv, head_chunks, seg_rows, paired);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kWarps * 32);
+  cfg.dynamicSmemBytes = Cfg::kSmem;
+  cfg.stream = a.stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, a, tk, tv, head_chunks, seg_rows, paired);
 }
 
 template <typename T, int D>

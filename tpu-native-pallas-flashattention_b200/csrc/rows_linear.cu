@@ -21,6 +21,11 @@
 // round trip), normalises the 16 rows while they are in flight, and runs
 // m16n8k16 MMAs.
 //
+// Each launch is a programmatic dependent launch: its CTAs may start while the
+// previous kernel on the stream finishes, issue their (constant) weight loads,
+// and wait (griddepcontrol.wait) before reading activations or writing
+// anything; the kernel lets its own dependents launch right after that wait.
+//
 // CTA = 32 output columns (16 in mode 2: 16 gate + 16 up weight rows), 8 warps
 // that split K in 32-element units; the warps' fp32 partials are summed in a
 // fixed order in shared memory (deterministic).  Inside a 32-element unit a
@@ -111,6 +116,13 @@ rows_linear_kernel(const T* __restrict__ x, const T* __restrict__ norm_w, float 
         bq[i][t] = __ldg(reinterpret_cast<const uint4*>(wt + (size_t)wrow[t] * K + (u0 + i) * 32 + 8 * c));
     }
   }
+
+  // Launched as a programmatic dependent of the previous kernel on the stream:
+  // the weights above are constants, everything below reads or writes data
+  // that kernel may produce or consume, so wait for its completion here.  The
+  // next kernel may launch now (it waits the same way before touching ours).
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   // The epilogue's residual values (mode 1) are fetched now as well.
   T resv[2];
@@ -289,9 +301,20 @@ static cudaError_t launch_rl(const void* x, const void* norm_w, float eps, const
   do {                                                                                                           \
     cudaError_t e = ensure_smem(rows_linear_kernel<T, U>, (int)rows_linear_smem(kRlWarps * (U) * 32));         \
     if (e != cudaSuccess) return e;                                                                              \
-    rows_linear_kernel<T, U><<<grid, kRlThreads, smem, st>>>(                                                    \
-        static_cast<const T*>(x), static_cast<const T*>(norm_w), eps, static_cast<const T*>(wt),                 \
-        static_cast<const T*>(res), static_cast<T*>(y), M, K, N, mode, rp);                                      \
+    cudaLaunchConfig_t cfg = {};                                                                                 \
+    cfg.gridDim = dim3(grid);                                                                                    \
+    cfg.blockDim = dim3(kRlThreads);                                                                             \
+    cfg.dynamicSmemBytes = smem;                                                                                 \
+    cfg.stream = st;                                                                                             \
+    cudaLaunchAttribute attr[1];                                                                                 \
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;                                             \
+    attr[0].val.programmaticStreamSerializationAllowed = 1;                                                      \
+    cfg.attrs = attr;                                                                                            \
+    cfg.numAttrs = 1;                                                                                            \
+    e = cudaLaunchKernelEx(&cfg, rows_linear_kernel<T, U>, static_cast<const T*>(x),                             \
+                           static_cast<const T*>(norm_w), eps, static_cast<const T*>(wt),                        \
+                           static_cast<const T*>(res), static_cast<T*>(y), M, K, N, mode, rp);                   \
+    if (e != cudaSuccess) return e;                                                                              \
   } while (0)
 #define PF_RL_U(T)                              \
   do {                                          \
