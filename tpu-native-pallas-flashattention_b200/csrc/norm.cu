@@ -170,10 +170,39 @@ argmax_embed_kernel(const T* __restrict__ logits, long row_stride, int vocab, in
   const int b = blockIdx.x;
   const T* row = logits + (long)b * row_stride;
   ArgBest best{-INFINITY, INT_MAX, false};
-  for (int v = threadIdx.x; v < vocab; v += kArgThreads) {
-    const float f = to_f(row[v]);
-    const ArgBest c{f, v, f != f};
-    if (arg_beats(c, best)) best = c;
+  constexpr int E = 16 / sizeof(T);  // elements per 16-byte vector
+  if (reinterpret_cast<uintptr_t>(row) % 16 == 0 && vocab % E == 0) {
+    // 16-byte loads, four vectors per thread in flight before any compare
+    // (arg_beats orders candidates by value, then index, so the scan order
+    // does not change the winner).
+    const int nvec = vocab / E;
+    const uint4* rv = reinterpret_cast<const uint4*>(row);
+    for (int base = threadIdx.x; base < nvec; base += 4 * kArgThreads) {
+      uint4 q[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int iv = base + u * kArgThreads;
+        q[u] = iv < nvec ? rv[iv] : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int iv = base + u * kArgThreads;
+        if (iv >= nvec) continue;
+        const T* e = reinterpret_cast<const T*>(&q[u]);
+#pragma unroll
+        for (int k = 0; k < E; ++k) {
+          const float f = to_f(e[k]);
+          const ArgBest c{f, iv * E + k, f != f};
+          if (arg_beats(c, best)) best = c;
+        }
+      }
+    }
+  } else {
+    for (int v = threadIdx.x; v < vocab; v += kArgThreads) {
+      const float f = to_f(row[v]);
+      const ArgBest c{f, v, f != f};
+      if (arg_beats(c, best)) best = c;
+    }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
