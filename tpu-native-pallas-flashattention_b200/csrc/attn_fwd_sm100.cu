@@ -432,6 +432,7 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     const uint32_t o_addr = lane_base + (w == 0 ? Cfg::kO0 : Cfg::kO1);
     bool ok = true;
     int cnt = 0, n_done = 0;  // S/P tiles of this slot and non-empty items so far
+    bool rotated_ahead = false;  // this item's query tile was rotated before the previous epilogue
     for (int r = 0; ok && r * (int)gridDim.x < n_items; ++r) {
       const int item = serpentine(r);
       if (item >= n_items) continue;
@@ -440,7 +441,7 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       const int n = t.n_w[w];
       const int q_start = t.q_start, kv_len = t.kv_len, q_off = t.q_off;
       const int qpos = q_start + w * kBM + row;
-      if (ROPE && n > 0) {
+      if (ROPE && n > 0 && !rotated_ahead) {
         // Rotate this warpgroup's query tile once, before any S MMA reads it.
         ok = mbar_wait(&bars->q, n_done & 1);
         if (ok && qpos < Sq)
@@ -547,6 +548,28 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         tc_fence_before();
         if (threadIdx.x == 0 || threadIdx.x == 128) trace(9 + 2 * w, j);
         mbar_arrive(&bars->p_full[w]);
+      }
+      // RoPE: the next item's query tile lands once this item's S MMAs are done
+      // (q_empty); rotating it now, before this item's epilogue, lets the
+      // next item's first S MMAs run under the epilogue instead of after it.
+      if (ROPE) {
+        rotated_ahead = false;
+        for (int r2 = r + 1; ok && r2 * (int)gridDim.x < n_items; ++r2) {
+          const int item2 = serpentine(r2);
+          if (item2 >= n_items) continue;
+          const FwdItem t2 = item_at(item2);
+          if (t2.n_max == 0) continue;
+          if (t2.n_w[w] > 0) {
+            ok = mbar_wait(&bars->q, (n_done + 1) & 1);
+            const int qpos2 = t2.q_start + w * kBM + row;
+            if (ok && qpos2 < Sq)
+              rope_row_in_smem<T, D>(smem + Cfg::kQOff + w * Cfg::kTileBytes, row, q_cos, q_sin, tbl_dtype, qpos2);
+            fence_proxy_async_smem();
+            mbar_arrive(&bars->q_ready[w]);
+            rotated_ahead = true;
+          }
+          break;
+        }
       }
       // ---------------------------- epilogue ----------------------------
       if (n > 0) {
