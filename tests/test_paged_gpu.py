@@ -326,6 +326,8 @@ def _prefill_oracle(q, k_pages, v_pages, tables, lens):
     (8, 2, 64, 32, [40, 512], 40),
     (4, 4, 128, 16, [1000, 129], 129),
     (2, 1, 128, 8, [257], 256),
+    (4, 2, 128, 128, [300, 1000, 77], 64),
+    (8, 2, 64, 256, [40, 700], 40),
 ])
 def test_paged_prefill_matches_oracle(dtype, H, Hkv, D, ps, lens, L):
     B = len(lens)
@@ -372,6 +374,33 @@ def test_paged_prefill_reads_no_ungathered_workspace_row(dtype):
     want = _prefill_oracle(widen(tq), widen(tk), widen(tv), tables, lens)
     tol = 2e-3 if dtype == torch.float32 else 2e-2
     assert np.max(np.abs(got - want)) < tol
+
+
+@pytest.mark.parametrize("ps", [8, 16, 128])
+def test_paged_prefill_ignores_pool_rows_past_the_context(ps):
+    """Rows at or past a sequence's length (the rest of its last page, pages it does
+    not own) are NaN-poisoned, so reading or multiplying any of them shows up as NaN:
+    the context gather must copy only live rows and zero-fill the rest of the tile."""
+    dtype = torch.bfloat16
+    H, Hkv, D, L = 4, 2, 128, 48
+    lens = [700, 49, 130, 256]
+    B = len(lens)
+    pps = max((n + ps - 1) // ps for n in lens) + 2
+    num_pages = B * pps + 5
+    tables = scrambled_table(B, pps, num_pages, seed=17)
+    q, kp, vp = randn((B, H, L, D), 61), randn((num_pages, Hkv, ps, D), 62), randn((num_pages, Hkv, ps, D), 63)
+    live = np.zeros((num_pages, ps), dtype=bool)
+    for b, n in enumerate(lens):
+        for t in range(n):
+            live[tables[b, t // ps], t % ps] = True
+    kp = np.where(live[:, None, :, None], kp, np.nan)
+    vp = np.where(live[:, None, :, None], vp, np.nan)
+    tq, tk, tv = to_dev(q, dtype), to_dev(kp, dtype), to_dev(vp, dtype)
+    got = pf.paged_prefill_attention(tq, tk, tv, torch.from_numpy(tables), torch.tensor(lens, dtype=torch.int32))
+    out = to_np(got)
+    assert np.isfinite(out).all()
+    want = _prefill_oracle(widen(tq), widen(tk), widen(tv), tables, lens)
+    assert np.max(np.abs(out - want)) < 2e-2
 
 
 def test_paged_prefill_single_token_equals_paged_decode():
